@@ -1,0 +1,330 @@
+"""Benchmark of the fp32 GEMM path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl jstorch|reference]
+
+Workload (the BASELINE metric "fp32 GEMM TFLOP/s at 8192^3 (1 GPU, % roofline);
+1/2/4/8-GPU sharded scaling"):
+  * N = 1: configuration 3, C = A.B with M = N = K = 8192, A, B ~ N(0, 1),
+    seed 2, device-resident, through the library's GEMM entry point.
+  * N > 1: the row-sharded GEMM of configuration 5 with 8192 rows of A per
+    rank (M = 8192 N, K = N = 8192; at N = 8 exactly configuration 5's
+    65536 x 8192 x 8192): B broadcast, each rank multiplies its row block,
+    C all-gathered.  Per-GPU work is fixed as N grows ("scaling": "weak").
+A step is one pass of the hot path over one batch of input: one GEMM call.
+
+Reported: `value` = device-timed TFLOP/s of the whole job (inputs resident in
+HBM, max over ranks); `e2e` = the same GEMM through the host-array entry point
+(jst_matmul_host_async: pinned host A, B in, C out, copies inside the timed
+region); `roofline` of the dominant kernel (tc_gemm) timed live with CUDA
+events on its own stream; `cpu_baseline` = the reference's CPU path (an fp32
+triple loop; the reference has no CPU implementation) on a bounded sample.
+
+`--impl reference` times that CPU path alone, with all host threads, on the
+same workload and metric (rank 0 only; other ranks exit at once).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SIZE = 8192
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16_tflops": d["bf16_tflops"], "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _traffic_from_profiles() -> tuple[float | None, str | None]:
+    """DRAM bytes per tc_gemm launch at 8192^3 from the committed ncu summary."""
+    p = ROOT / "profiles" / "tc_gemm_8192.json"
+    if not p.exists():
+        return None, None
+    d = json.loads(p.read_text())
+    return d.get("dram_bytes_per_launch"), d.get("source")
+
+
+def cpu_baseline(A: np.ndarray, B: np.ndarray, target_s: float = 12.0) -> dict:
+    """The reference's CPU path (fp32 i-k-j triple loop, OpenMP over rows, all
+    host threads) on the first R rows of C, R sized for ~target_s seconds."""
+    from oracle import oracle
+
+    M, K = A.shape
+    N = B.shape[1]
+    C = np.zeros((M, N), np.float32)
+    t0 = time.perf_counter()
+    threads = oracle.sgemm_f32_cpu(A, B, C, 0, 8)
+    dt = max(time.perf_counter() - t0, 1e-6)
+    rate = 8 / dt  # rows per second
+    rows = int(max(8, min(M, rate * target_s)))
+    t0 = time.perf_counter()
+    oracle.sgemm_f32_cpu(A, B, C, 0, rows)
+    dt = time.perf_counter() - t0
+    tflops = 2.0 * rows * N * K / dt / 1e12
+    return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"first {rows} of {M} rows of C ({rows}x{N}x{K} fp32 i-k-j loop, {dt:.1f} s; "
+                      f"rate extrapolated to the full GEMM)",
+            "seconds": dt}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from jstorch_b200 import synth
+    from oracle import oracle
+
+    A, B = synth.config3()
+    M, K = A.shape
+    N = B.shape[1]
+    C = np.zeros((M, N), np.float32)
+    # size one step to ~4 s of CPU work
+    t0 = time.perf_counter()
+    threads = oracle.sgemm_f32_cpu(A, B, C, 0, 8)
+    rate = 8 / max(time.perf_counter() - t0, 1e-6)
+    rows = int(max(8, min(M, rate * 4.0)))
+    for w in range(args.warmup):
+        oracle.sgemm_f32_cpu(A, B, C, 0, min(rows, 8))
+    times = []
+    for s in range(args.steps):
+        r0 = (s * rows) % max(M - rows + 1, 1)
+        t0 = time.perf_counter()
+        oracle.sgemm_f32_cpu(A, B, C, r0, rows)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    flops = 2.0 * rows * N * K * args.steps
+    tflops = flops / total / 1e12
+    ms_full = 2.0 * M * N * K / (tflops * 1e12) * 1e3
+    line = {
+        "impl": "reference", "metric": "fp32 GEMM TFLOP/s at 8192^3", "value": tflops, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_full,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (numpy PCG64, seed 2)",
+        "config": {"workload": "config3: C=A.B, M=N=K=8192, A,B~N(0,1), row-major fp32",
+                   "sample_per_step": f"{rows} rows of C", "parallelism": "host threads"},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows of C per step ({rows}x{N}x{K}), {args.steps} steps, "
+                                   f"fp32 i-k-j loop (the reference has no CPU path; this is its row-major "
+                                   f"fp32 loop)"},
+        "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_jstorch(args) -> None:
+    import torch
+
+    import jstorch_b200
+    from jstorch_b200 import _lib, synth
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        raise SystemExit("multi-GPU bench not built yet")
+
+    M = N = K = SIZE
+    A, B = synth.config3()
+    a = torch.from_numpy(A).to(dev)
+    b = torch.from_numpy(B).to(dev)
+    c = torch.empty((M, N), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    flops = 2.0 * M * N * K
+
+    # ---- device-resident timing (value) + live kernel timing (roofline)
+    for _ in range(args.warmup):
+        jstorch_b200.gemm(a, b, out=c, kernel=args.kernel)
+    torch.cuda.synchronize()
+    n0 = _lib.launch_count()
+    _lib.profile_enable(True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        jstorch_b200.gemm(a, b, out=c, kernel=args.kernel)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = _lib.launch_count() - n0
+    kstats = _lib.profile_read()
+    _lib.profile_enable(False)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    value = flops / (ms * 1e-3) / 1e12
+    if jstorch_b200.device_error():
+        raise SystemExit("device error word set during the benchmark")
+
+    # ---- end to end through the host-array entry point (pinned host buffers)
+    a_h = torch.from_numpy(A).pin_memory()
+    b_h = torch.from_numpy(B).pin_memory()
+    c_h = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    for _ in range(max(1, args.warmup)):
+        jstorch_b200.matmul_host_async(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, K, N, stream)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        jstorch_b200.matmul_host_async(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, K, N, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": int(A.nbytes + B.nbytes), "d2h_bytes_per_step": int(M * N * 4),
+           "api": "jst_matmul_host_async (torch.matmul(a, b, M, K, N) entry point), pinned host buffers"}
+
+    # ---- roofline of the dominant kernel
+    peaks = _peaks()
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    top = max(kstats.items(), key=lambda kv: kv[1][1]) if kstats else ("none", (0, 0.0))
+    name, (nl, tot) = top
+    kernel_ms = tot / max(nl, 1)
+    achieved = flops / (kernel_ms * 1e-3) / 1e12 if kernel_ms > 0 else None
+    traffic, traffic_src = _traffic_from_profiles()
+    roofline = {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": tf32_peak / 3.0,
+                "unit": "TFLOP/s", "frac": (achieved / (tf32_peak / 3.0)) if achieved else None,
+                "traffic": traffic,
+                "peak_note": f"3xTF32 roofline = (dense bf16 {peaks['bf16_tflops']} TF/s {peaks['source']}, "
+                             f"burst) / 2 (TF32 rate) / 3 (three products)",
+                "traffic_note": traffic_src,
+                "kernel_ms": kernel_ms,
+                "kernels": {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in kstats.items()}}
+
+    # ---- reference GPU library path (cuBLAS sgemm with TF32 math, as the
+    # reference configures it) on the same inputs, for context
+    ref_gpu = None
+    try:
+        torch.backends.cuda.matmul.allow_tf32 = True
+        for _ in range(2):
+            torch.matmul(a, b, out=c)
+        torch.cuda.synchronize()
+        r0 = torch.cuda.Event(enable_timing=True)
+        r1 = torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        for _ in range(args.steps):
+            torch.matmul(a, b, out=c)
+        r1.record(stream)
+        torch.cuda.synchronize()
+        torch.backends.cuda.matmul.allow_tf32 = False
+        ref_ms = r0.elapsed_time(r1) / args.steps
+        ref_gpu = {"impl": "cuBLAS sgemm, TF32 tensor-op math (reference native/ops/matmul.cu:12)",
+                   "tflops": flops / (ref_ms * 1e-3) / 1e12, "ms": ref_ms}
+    except Exception as e:  # context only; never fatal
+        ref_gpu = {"error": str(e)}
+
+    line = {
+        "metric": "fp32 GEMM TFLOP/s at 8192^3", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (numpy PCG64, seed 2)",
+        "config": {"workload": "config3: C=A.B, M=N=K=8192, A,B~N(0,1), row-major fp32, device-resident",
+                   "kernel": args.kernel, "parallelism": "single GPU",
+                   "l2": "inputs larger than L2 (A, B, C 256 MiB each; split planes 1 GiB)"},
+        "e2e": e2e, "roofline": roofline, "gpu_launches": launches, "clocks": clk,
+        "reference_gpu_library": ref_gpu,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(A, B)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["jstorch", "reference"], default="jstorch")
+    ap.add_argument("--kernel", choices=["auto", "tc3xtf32", "ffma"], default="auto")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_jstorch(args)
+
+
+if __name__ == "__main__":
+    main()

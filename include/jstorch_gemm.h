@@ -1,0 +1,156 @@
+/*
+ * jstorch_gemm.h -- C ABI of the B200 (sm_100a) fp32 GEMM library that
+ * replaces JsTorch's cuBLAS matmul path.
+ *
+ * Library: jstorch_b200/libjstorch_gemm.so.  Plain C linkage, plain pointers
+ * and sizes.  All matrices are fp32 and row-major, as in JsTorch.
+ *
+ * Reference interfaces replaced (paths relative to the JsTorch project root):
+ *   launch_matmul  native/ops/matmul.cu:28   (declared native/core/tensor.cpp:69)
+ *   launch_bmm     native/ops/matmul.cu:40   (declared native/core/tensor.cpp:71)
+ *   launch_linear  native/ops/matmul.cu:54   (declared native/core/tensor.cpp:70)
+ * They keep the reference signatures and `void` return, so tensor.cpp links
+ * against this library unchanged; their status is readable afterwards through
+ * jst_get_last_status().  Everything else here is new surface that the
+ * reference does not have (it has no status codes, no NT/TN forms, no
+ * epilogue options and no multi-GPU path).
+ */
+#ifndef JSTORCH_GEMM_H
+#define JSTORCH_GEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers (same type). */
+typedef struct CUstream_st* jst_stream_t;
+
+/* ---------------------------------------------------------------- status */
+typedef enum jst_status {
+    JST_OK = 0,
+    JST_ERR_ARG = 1,          /* bad shape, stride, pointer or enum value        */
+    JST_ERR_ALIGN = 2,        /* a forced kernel cannot take this alignment      */
+    JST_ERR_CUDA = 3,         /* a CUDA runtime call or launch failed            */
+    JST_ERR_NCCL = 4,         /* an NCCL call failed                             */
+    JST_ERR_TIMEOUT = 5,      /* a bounded device or host wait gave up           */
+    JST_ERR_UNSUPPORTED = 6,  /* no kernel of this build can run the request     */
+    JST_ERR_NOMEM = 7,        /* device or pinned host allocation failed         */
+    JST_ERR_NO_DEVICE = 8     /* no CUDA device of compute capability 10.x       */
+} jst_status;
+
+/* Human-readable text of the last non-OK status raised on the calling thread. */
+const char* jst_last_error(void);
+/* Status of the last call made on the calling thread (for the void launchers). */
+int jst_get_last_status(void);
+
+/* ---------------------------------------------------------------- GEMM */
+typedef enum jst_epilogue {
+    JST_EPI_NONE = 0,
+    JST_EPI_BIAS = 1,       /* C[i,j] = acc + bias[j]            */
+    JST_EPI_RELU = 2,       /* C[i,j] = max(acc, 0)              */
+    JST_EPI_BIAS_RELU = 3   /* C[i,j] = max(acc + bias[j], 0)    */
+} jst_epilogue;
+
+typedef enum jst_kernel {
+    JST_KERNEL_AUTO = 0,      /* shape heuristic                                  */
+    JST_KERNEL_TC3XTF32 = 1,  /* tcgen05/TMEM split-precision (3 x TF32) kernel   */
+    JST_KERNEL_FFMA = 2       /* fp32 FFMA SIMT kernel                            */
+} jst_kernel;
+
+/*
+ * C[b] = epilogue( op(A[b]) * op(B[b]) ),  b = 0 .. batch-1
+ *   op(A) is [M, K]: transA = 0 -> A stored [M, K] (lda >= K),
+ *                    transA = 1 -> A stored [K, M] (lda >= M).
+ *   op(B) is [K, N]: transB = 0 -> B stored [K, N] (ldb >= N),
+ *                    transB = 1 -> B stored [N, K] (ldb >= K).
+ *   C is [M, N] with ldc >= N.  Strides are in elements; batch strides may be 0
+ *   (broadcast operand).  All pointers are device pointers of the current device.
+ *   The call is asynchronous on `stream` (NULL = legacy default stream, as the
+ *   reference uses).  M, N or K of 0 is legal: K == 0 writes epilogue(0).
+ */
+typedef struct jst_gemm_desc {
+    int transA, transB;
+    int M, N, K;
+    const float* A; int64_t lda; int64_t strideA;
+    const float* B; int64_t ldb; int64_t strideB;
+    float* C;       int64_t ldc; int64_t strideC;
+    int batch;                 /* >= 1                                            */
+    const float* bias;         /* [N], required for the *_BIAS* epilogues         */
+    int epilogue;              /* jst_epilogue                                    */
+    int kernel;                /* jst_kernel                                      */
+    jst_stream_t stream;
+} jst_gemm_desc;
+
+/* Fill a descriptor for a packed row-major C = A*B (NN, batch 1, no epilogue). */
+void jst_gemm_desc_init(jst_gemm_desc* d, int M, int N, int K,
+                        const float* A, const float* B, float* C);
+
+int jst_gemm_ex(const jst_gemm_desc* d);
+
+/* Which kernel JST_KERNEL_AUTO would run for `d` (JST_KERNEL_TC3XTF32 or _FFMA). */
+int jst_gemm_select_kernel(const jst_gemm_desc* d);
+
+/* ------------------------------------------- reference-compatible launchers */
+/* native/ops/matmul.cu:28 -- row-major [M,K] x [K,N] -> [M,N] */
+void launch_matmul(const float* a, const float* b, float* c, int M, int K, int N, jst_stream_t s);
+/* native/ops/matmul.cu:40 -- [B,M,K] x [B,K,N] -> [B,M,N], packed strides */
+void launch_bmm(const float* a, const float* b, float* c, int B, int M, int K, int N, jst_stream_t s);
+/* native/ops/matmul.cu:54 -- out[B,out_f] = x[B,in_f] * w[out_f,in_f]^T + bias (nullable) */
+void launch_linear(const float* x, const float* w, const float* bias, float* out,
+                   int B, int in_f, int out_f, jst_stream_t s);
+
+/* --------------------------------------------- torch.matmul(a, b, M, K, N) */
+/*
+ * README.md:37-84 of the reference documents torch.matmul(a, b, M, K, N) on
+ * row-major Float32Array returning a Float32Array; the code base never
+ * implemented it.  This is the native entry point an N-API shim binds: HOST
+ * pointers in and out, staged through cached pinned buffers, computed on the
+ * current device, synchronous on return.  c must hold M*N floats.
+ */
+int jst_matmul_host(const float* a, const float* b, float* c, int M, int K, int N);
+
+/*
+ * Stream-ordered form of jst_matmul_host (no counterpart in the reference):
+ * enqueues the host->device copies, the GEMM and the device->host copy on
+ * `stream` and returns.  With pinned (page-locked) host buffers the call is
+ * asynchronous and `c` is valid once the stream reaches that point; with
+ * pageable buffers the copies synchronise as cudaMemcpyAsync does.  The
+ * device staging buffers are per device: calls on different streams of the
+ * same device must not overlap in time.
+ */
+int jst_matmul_host_async(const float* a, const float* b, float* c, int M, int K, int N, jst_stream_t stream);
+
+/* ---------------------------------------------------- device-side status */
+/*
+ * Kernels never trap: a pipeline wait that exceeds its bound sets a device
+ * error word and the kernel exits.  jst_device_error() synchronises the
+ * current device and returns (and clears) that word: 0 = none, 1 = timeout.
+ */
+int jst_device_error(void);
+
+/* Release cached device workspace and pinned staging buffers of this process. */
+void jst_release_caches(void);
+
+/* ------------------------------------------------------------ profiling */
+/* (no counterpart in the reference, which has no tracing) */
+typedef struct jst_kernel_stat {
+    char name[32];       /* kernel family: tc_gemm, split_rows, ffma_gemm, ...  */
+    int64_t launches;
+    double total_ms;     /* summed device time between the bracketing events   */
+} jst_kernel_stat;
+
+/* Number of kernels this library has launched in the process so far. */
+int64_t jst_launch_count(void);
+/* on != 0: bracket every launch with CUDA events on its stream.  Resets stats. */
+int jst_profile_enable(int on);
+/* Wait for the recorded events and fill up to max_entries stats; returns the
+ * number of kernel families seen (or -status on a CUDA error). */
+int jst_profile_read(jst_kernel_stat* out, int max_entries);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JSTORCH_GEMM_H */

@@ -1,0 +1,345 @@
+// gemm_api.cu -- the C ABI of libjstorch_gemm.so (declared in
+// include/jstorch_gemm.h): argument validation, kernel selection, workspace,
+// status reporting, the reference-compatible launchers and the host-array
+// torch.matmul entry point.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "gemm_internal.h"
+
+namespace jst {
+
+// ---------------------------------------------------------------- status
+static thread_local int t_status = JST_OK;
+static thread_local char t_msg[256] = "";
+
+int set_status(int status, const char* msg) {
+    t_status = status;
+    if (status != JST_OK) {
+        std::snprintf(t_msg, sizeof(t_msg), "%s", msg ? msg : "");
+    }
+    return status;
+}
+
+static int cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return JST_OK;
+    char buf[256];
+    std::snprintf(buf, sizeof(buf), "%s: %s", what, cudaGetErrorString(e));
+    return set_status(e == cudaErrorMemoryAllocation ? JST_ERR_NOMEM : JST_ERR_CUDA, buf);
+}
+
+// ---------------------------------------------------------------- devices
+struct DeviceState {
+    bool init = false;
+    bool ok = false;
+    uint32_t* err_word = nullptr;
+    cudaMemPool_t pool = nullptr;
+};
+static std::mutex g_dev_mu;
+static DeviceState g_dev[64];
+
+// Validates that the current device is a compute-capability 10.x part and
+// sets up its error word and workspace pool once.
+static int current_device(int* out_dev) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return set_status(JST_ERR_NO_DEVICE, "no CUDA device available");
+    }
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DeviceState& st = g_dev[dev];
+    if (!st.init) {
+        st.init = true;
+        int major = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        if (major != 10) {
+            cudaGetLastError();
+            return set_status(JST_ERR_NO_DEVICE, "libjstorch_gemm is built for sm_100a (B200) only");
+        }
+        if (cudaMalloc(&st.err_word, sizeof(uint32_t)) != cudaSuccess ||
+            cudaMemset(st.err_word, 0, sizeof(uint32_t)) != cudaSuccess) {
+            cudaGetLastError();
+            return set_status(JST_ERR_NOMEM, "cannot allocate the device error word");
+        }
+        cudaMemPoolProps props;
+        std::memset(&props, 0, sizeof(props));
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        if (cudaMemPoolCreate(&st.pool, &props) != cudaSuccess) {
+            cudaGetLastError();
+            return set_status(JST_ERR_CUDA, "cudaMemPoolCreate failed");
+        }
+        uint64_t keep = ~0ull;  // cache freed workspace inside the pool
+        cudaMemPoolSetAttribute(st.pool, cudaMemPoolAttrReleaseThreshold, &keep);
+        st.ok = true;
+    }
+    if (!st.ok) return set_status(JST_ERR_NO_DEVICE, "device unusable by libjstorch_gemm (see first error)");
+    *out_dev = dev;
+    return JST_OK;
+}
+
+uint32_t* device_error_word() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return (dev >= 0 && dev < 64) ? g_dev[dev].err_word : nullptr;
+}
+
+// ---------------------------------------------------------------- dispatch
+static bool use_tc(const GemmArgs& a) {
+    // The split pass costs one read of each operand plus two plane writes; the
+    // tensor-core kernel needs whole 128 x 256 tiles to pay for it.
+    const double macs = (double)a.M * a.N * a.K * a.batch;
+    return a.M >= 64 && a.N >= 64 && a.K >= 32 && macs >= 32.0e6;
+}
+
+static int validate(const jst_gemm_desc* d, GemmArgs* a) {
+    if (!d) return set_status(JST_ERR_ARG, "null descriptor");
+    if (d->M < 0 || d->N < 0 || d->K < 0) return set_status(JST_ERR_ARG, "negative dimension");
+    if (d->batch < 1) return set_status(JST_ERR_ARG, "batch must be >= 1");
+    if (d->transA != 0 && d->transA != 1) return set_status(JST_ERR_ARG, "transA must be 0 or 1");
+    if (d->transB != 0 && d->transB != 1) return set_status(JST_ERR_ARG, "transB must be 0 or 1");
+    if (d->epilogue < JST_EPI_NONE || d->epilogue > JST_EPI_BIAS_RELU)
+        return set_status(JST_ERR_ARG, "unknown epilogue");
+    if (d->kernel < JST_KERNEL_AUTO || d->kernel > JST_KERNEL_FFMA) return set_status(JST_ERR_ARG, "unknown kernel");
+    const bool has_bias = d->epilogue == JST_EPI_BIAS || d->epilogue == JST_EPI_BIAS_RELU;
+    if (has_bias && !d->bias) return set_status(JST_ERR_ARG, "bias epilogue without a bias pointer");
+    const int64_t a_rows = d->transA ? d->K : d->M, a_cols = d->transA ? d->M : d->K;
+    const int64_t b_rows = d->transB ? d->N : d->K, b_cols = d->transB ? d->K : d->N;
+    if (d->M > 0 && d->N > 0) {
+        if (!d->C) return set_status(JST_ERR_ARG, "null C");
+        if (d->ldc < d->N) return set_status(JST_ERR_ARG, "ldc < N");
+        if (d->batch > 1 && d->strideC < (int64_t)(d->M - 1) * d->ldc + d->N)
+            return set_status(JST_ERR_ARG, "strideC overlaps batches of C");
+        if (d->K > 0) {
+            if (!d->A || !d->B) return set_status(JST_ERR_ARG, "null A or B");
+            if (d->lda < std::max<int64_t>(a_cols, 1)) return set_status(JST_ERR_ARG, "lda too small");
+            if (d->ldb < std::max<int64_t>(b_cols, 1)) return set_status(JST_ERR_ARG, "ldb too small");
+            if (d->strideA < 0 || d->strideB < 0) return set_status(JST_ERR_ARG, "negative batch stride");
+            (void)a_rows; (void)b_rows;
+        }
+    }
+    a->transA = d->transA; a->transB = d->transB;
+    a->M = d->M; a->N = d->N; a->K = d->K; a->batch = d->batch;
+    a->A = d->A; a->lda = d->lda; a->strideA = d->strideA;
+    a->B = d->B; a->ldb = d->ldb; a->strideB = d->strideB;
+    a->C = d->C; a->ldc = d->ldc; a->strideC = d->strideC;
+    a->bias = has_bias ? d->bias : nullptr;
+    a->relu = (d->epilogue == JST_EPI_RELU || d->epilogue == JST_EPI_BIAS_RELU) ? 1 : 0;
+    return JST_OK;
+}
+
+static int gemm(const jst_gemm_desc* d) {
+    GemmArgs a;
+    int rc = validate(d, &a);
+    if (rc) return rc;
+    int dev = 0;
+    rc = current_device(&dev);
+    if (rc) return rc;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(d->stream);
+    if (a.M == 0 || a.N == 0) return set_status(JST_OK, nullptr);
+    if (a.K == 0) {
+        rc = fill_epilogue_run(a, s);
+        return rc ? rc : set_status(JST_OK, nullptr);
+    }
+    const int k = d->kernel == JST_KERNEL_AUTO ? (use_tc(a) ? JST_KERNEL_TC3XTF32 : JST_KERNEL_FFMA) : d->kernel;
+    if (k == JST_KERNEL_FFMA) {
+        rc = ffma_gemm_run(a, s);
+        return rc ? rc : set_status(JST_OK, nullptr);
+    }
+    // tensor-core path: stream-ordered workspace from this library's pool
+    const size_t bytes = tc_workspace_bytes(a);
+    void* ws = nullptr;
+    rc = cuda_status(cudaMallocFromPoolAsync(&ws, bytes, g_dev[dev].pool, s), "workspace allocation");
+    if (rc) return rc;
+    rc = tc_gemm_run(a, ws, s);
+    cudaError_t fe = cudaFreeAsync(ws, s);
+    if (rc) return rc;
+    rc = cuda_status(fe, "workspace release");
+    return rc ? rc : set_status(JST_OK, nullptr);
+}
+
+// ---------------------------------------------------------------- host staging
+struct HostStage {
+    std::mutex mu;
+    int dev = -1;
+    cudaStream_t stream = nullptr;
+    float* d_buf = nullptr;  // A | B | C
+    size_t d_cap = 0;        // floats
+};
+static HostStage g_host[64];
+
+// Host-array GEMM: stage a and b to device buffers cached per device, run the
+// GEMM, copy C back.  `stream` == nullptr uses the library's own stream and
+// waits for completion; otherwise everything is enqueued on `stream`.
+static int host_matmul(const float* a, const float* b, float* c, int M, int K, int N, cudaStream_t user_stream) {
+    if (M < 0 || K < 0 || N < 0) return set_status(JST_ERR_ARG, "negative dimension");
+    if ((M > 0 && K > 0 && !a) || (K > 0 && N > 0 && !b) || (M > 0 && N > 0 && !c))
+        return set_status(JST_ERR_ARG, "null host pointer");
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    HostStage& h = g_host[dev];
+    std::lock_guard<std::mutex> lk(h.mu);
+    if (!user_stream && !h.stream) {
+        rc = cuda_status(cudaStreamCreateWithFlags(&h.stream, cudaStreamNonBlocking), "stream create");
+        if (rc) return rc;
+    }
+    cudaStream_t st = user_stream ? user_stream : h.stream;
+    const size_t na = (size_t)M * K, nb = (size_t)K * N, nc = (size_t)M * N;
+    // keep each plane 16-byte aligned inside the staging buffer
+    auto up4 = [](size_t n) { return (n + 3) & ~size_t(3); };
+    const size_t need = up4(na) + up4(nb) + up4(nc);
+    if (need > h.d_cap) {
+        if (h.d_buf) {
+            cudaDeviceSynchronize();  // the old buffer may still be in use on some stream
+            cudaFree(h.d_buf);
+        }
+        h.d_buf = nullptr;
+        h.d_cap = 0;
+        rc = cuda_status(cudaMalloc(&h.d_buf, std::max<size_t>(need, 4) * sizeof(float)), "device staging");
+        if (rc) return rc;
+        h.d_cap = need;
+    }
+    float* dA = h.d_buf;
+    float* dB = dA + up4(na);
+    float* dC = dB + up4(nb);
+    if (na) {
+        rc = cuda_status(cudaMemcpyAsync(dA, a, na * sizeof(float), cudaMemcpyHostToDevice, st), "H2D A");
+        if (rc) return rc;
+    }
+    if (nb) {
+        rc = cuda_status(cudaMemcpyAsync(dB, b, nb * sizeof(float), cudaMemcpyHostToDevice, st), "H2D B");
+        if (rc) return rc;
+    }
+    jst_gemm_desc d;
+    jst_gemm_desc_init(&d, M, N, K, dA, dB, dC);
+    d.stream = reinterpret_cast<jst_stream_t>(st);
+    rc = gemm(&d);
+    if (rc) return rc;
+    if (nc) {
+        rc = cuda_status(cudaMemcpyAsync(c, dC, nc * sizeof(float), cudaMemcpyDeviceToHost, st), "D2H C");
+        if (rc) return rc;
+    }
+    if (user_stream) return set_status(JST_OK, nullptr);
+    rc = cuda_status(cudaStreamSynchronize(st), "matmul synchronise");
+    if (rc) return rc;
+    uint32_t* w = g_dev[dev].err_word;
+    uint32_t e = 0;
+    if (w && cudaMemcpy(&e, w, sizeof(e), cudaMemcpyDeviceToHost) == cudaSuccess && e != 0) {
+        cudaMemset(w, 0, sizeof(uint32_t));
+        return set_status(JST_ERR_TIMEOUT, "a GEMM kernel pipeline wait timed out");
+    }
+    return set_status(JST_OK, nullptr);
+}
+
+}  // namespace jst
+
+// ==================================================================== C ABI
+extern "C" {
+
+const char* jst_last_error(void) { return jst::t_msg; }
+int jst_get_last_status(void) { return jst::t_status; }
+
+void jst_gemm_desc_init(jst_gemm_desc* d, int M, int N, int K, const float* A, const float* B, float* C) {
+    if (!d) return;
+    std::memset(d, 0, sizeof(*d));
+    d->M = M; d->N = N; d->K = K;
+    d->A = A; d->lda = K; d->strideA = (int64_t)M * K;
+    d->B = B; d->ldb = N; d->strideB = (int64_t)K * N;
+    d->C = C; d->ldc = N; d->strideC = (int64_t)M * N;
+    d->batch = 1;
+    d->epilogue = JST_EPI_NONE;
+    d->kernel = JST_KERNEL_AUTO;
+    d->stream = nullptr;
+}
+
+int jst_gemm_ex(const jst_gemm_desc* d) { return jst::gemm(d); }
+
+int jst_gemm_select_kernel(const jst_gemm_desc* d) {
+    jst::GemmArgs a{};
+    if (jst::validate(d, &a)) return -1;
+    if (d->kernel != JST_KERNEL_AUTO) return d->kernel;
+    return jst::use_tc(a) ? JST_KERNEL_TC3XTF32 : JST_KERNEL_FFMA;
+}
+
+// native/ops/matmul.cu:28-37 -- row-major NN, beta = 0
+void launch_matmul(const float* a, const float* b, float* c, int M, int K, int N, jst_stream_t s) {
+    jst_gemm_desc d;
+    jst_gemm_desc_init(&d, M, N, K, a, b, c);
+    d.stream = s;
+    jst::gemm(&d);
+}
+
+// native/ops/matmul.cu:40-50 -- packed strided batch
+void launch_bmm(const float* a, const float* b, float* c, int B, int M, int K, int N, jst_stream_t s) {
+    jst_gemm_desc d;
+    jst_gemm_desc_init(&d, M, N, K, a, b, c);
+    d.batch = B;
+    d.stream = s;
+    jst::gemm(&d);
+}
+
+// native/ops/matmul.cu:54-67 -- out = x * w^T (+ bias), w stored [out_f, in_f]
+void launch_linear(const float* x, const float* w, const float* bias, float* out, int B, int in_f, int out_f,
+                   jst_stream_t s) {
+    jst_gemm_desc d;
+    jst_gemm_desc_init(&d, B, out_f, in_f, x, w, out);
+    d.transB = 1;
+    d.ldb = in_f;
+    d.strideB = (int64_t)out_f * in_f;
+    d.bias = bias;
+    d.epilogue = bias ? JST_EPI_BIAS : JST_EPI_NONE;
+    d.stream = s;
+    jst::gemm(&d);
+}
+
+int jst_matmul_host(const float* a, const float* b, float* c, int M, int K, int N) {
+    return jst::host_matmul(a, b, c, M, K, N, nullptr);
+}
+
+int jst_matmul_host_async(const float* a, const float* b, float* c, int M, int K, int N, jst_stream_t stream) {
+    if (!stream) return jst::set_status(JST_ERR_ARG, "jst_matmul_host_async needs a stream");
+    return jst::host_matmul(a, b, c, M, K, N, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int jst_device_error(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || !jst::g_dev[dev].err_word) {
+        cudaGetLastError();
+        return 0;
+    }
+    cudaDeviceSynchronize();
+    uint32_t e = 0;
+    cudaMemcpy(&e, jst::g_dev[dev].err_word, sizeof(e), cudaMemcpyDeviceToHost);
+    if (e) cudaMemset(jst::g_dev[dev].err_word, 0, sizeof(uint32_t));
+    return (int)e;
+}
+
+void jst_release_caches(void) {
+    int cur = 0;
+    if (cudaGetDevice(&cur) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    for (int i = 0; i < 64; ++i) {
+        std::lock_guard<std::mutex> lk(jst::g_host[i].mu);
+        if (!jst::g_host[i].d_buf && !jst::g_dev[i].pool) continue;
+        cudaSetDevice(i);
+        cudaDeviceSynchronize();
+        if (jst::g_host[i].d_buf) cudaFree(jst::g_host[i].d_buf);
+        jst::g_host[i].d_buf = nullptr;
+        jst::g_host[i].d_cap = 0;
+        if (jst::g_dev[i].pool) cudaMemPoolTrimTo(jst::g_dev[i].pool, 0);
+    }
+    cudaSetDevice(cur);
+}
+
+}  // extern "C"

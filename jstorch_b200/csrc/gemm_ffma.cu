@@ -1,0 +1,273 @@
+// gemm_ffma.cu -- fp32 FFMA (SIMT) GEMM for small and skinny shapes.
+//
+// Exact fp32 arithmetic (one fma per product, fp32 accumulation), no
+// workspace, all four layouts (op(A) = A or A^T, op(B) = B or B^T, the NN/NT/TN
+// forms of native/ops/matmul.cu:28-67 and of GradTensor::matmul_'s backward,
+// native/core/autograd.hpp:433-441), strided batches and the fused bias / ReLU
+// epilogue (matmul.cu:18-23, kernels.cuh:50).
+//
+// Register-blocked outer-product kernel: a CTA owns a BM x BN tile of C; each
+// thread owns (4*RM) x (4*RN) outputs laid out as RM x RN blocks of 4 x 4 that
+// sit BM/RM rows and BN/RN columns apart, so the shared-memory reads of a warp
+// are conflict-free float4 loads.  Tiles of A and B are staged k-major in
+// shared memory (double buffered; the next tile is fetched into registers
+// while the current one is multiplied).  Global loads are float4 whenever
+// the operand's leading dimension and base allow it, scalar and bounds-checked
+// elsewhere.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "gemm_internal.h"
+
+namespace jst {
+namespace ffma {
+
+struct Params {
+    int M, N, K;
+    const float* A; int64_t lda, strideA;
+    const float* B; int64_t ldb, strideB;
+    float* C; int64_t ldc, strideC;
+    const float* bias;
+    int relu;
+    int vecA, vecB, vecC;
+};
+
+template <int BM, int BN, int BK, int RM, int RN, bool TA, bool TB>
+__global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)))
+    ffma_gemm_kernel(const Params p) {
+    constexpr int TX = BN / (4 * RN);
+    constexpr int TY = BM / (4 * RM);
+    constexpr int NT = TX * TY;
+    constexpr int PAD = 4;
+    constexpr int A4 = BM * BK / 4;  // float4 slots per A tile
+    constexpr int B4 = BN * BK / 4;
+    constexpr int LA = (A4 + NT - 1) / NT;
+    constexpr int LB = (B4 + NT - 1) / NT;
+
+    __shared__ __align__(16) float As[2][BK][BM + PAD];
+    __shared__ __align__(16) float Bs[2][BK][BN + PAD];
+
+    const int tid = threadIdx.x;
+    const int tx = tid % TX;
+    const int ty = tid / TX;
+    const int m0 = blockIdx.y * BM;
+    const int n0 = blockIdx.x * BN;
+    const int b = blockIdx.z;
+    const float* A = p.A + (int64_t)b * p.strideA;
+    const float* B = p.B + (int64_t)b * p.strideB;
+    float* C = p.C + (int64_t)b * p.strideC;
+
+    float ra[LA][4], rb[LB][4];
+
+    // Fetch the k-slab starting at k0 into registers.
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int l = 0; l < LA; ++l) {
+            const int f = tid + l * NT;
+            int r, c;  // r: index along the contiguous-4 run's row, c: start of the run
+            if (!TA) { r = f / (BK / 4); c = (f % (BK / 4)) * 4; }   // row m, cols k..k+3
+            else     { r = f / (BM / 4); c = (f % (BM / 4)) * 4; }   // row k, cols m..m+3
+            const int gr = (!TA ? m0 : k0) + r;
+            const int gc = (!TA ? k0 : m0) + c;
+            const int rlim = !TA ? p.M : p.K;
+            const int clim = !TA ? p.K : p.M;
+            if (f < A4 && gr < rlim) {
+                const float* src = A + (int64_t)gr * p.lda + gc;
+                if (p.vecA && gc + 3 < clim) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(src));
+                    ra[l][0] = v.x; ra[l][1] = v.y; ra[l][2] = v.z; ra[l][3] = v.w;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) ra[l][j] = (gc + j < clim) ? __ldg(src + j) : 0.0f;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) ra[l][j] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int l = 0; l < LB; ++l) {
+            const int f = tid + l * NT;
+            int r, c;
+            if (!TB) { r = f / (BN / 4); c = (f % (BN / 4)) * 4; }   // row k, cols n..n+3
+            else     { r = f / (BK / 4); c = (f % (BK / 4)) * 4; }   // row n, cols k..k+3
+            const int gr = (!TB ? k0 : n0) + r;
+            const int gc = (!TB ? n0 : k0) + c;
+            const int rlim = !TB ? p.K : p.N;
+            const int clim = !TB ? p.N : p.K;
+            if (f < B4 && gr < rlim) {
+                const float* src = B + (int64_t)gr * p.ldb + gc;
+                if (p.vecB && gc + 3 < clim) {
+                    const float4 v = __ldg(reinterpret_cast<const float4*>(src));
+                    rb[l][0] = v.x; rb[l][1] = v.y; rb[l][2] = v.z; rb[l][3] = v.w;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) rb[l][j] = (gc + j < clim) ? __ldg(src + j) : 0.0f;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) rb[l][j] = 0.0f;
+            }
+        }
+    };
+
+    auto stash = [&](int buf) {
+#pragma unroll
+        for (int l = 0; l < LA; ++l) {
+            const int f = tid + l * NT;
+            if (f >= A4) continue;
+            if (!TA) {
+                const int m = f / (BK / 4), k = (f % (BK / 4)) * 4;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) As[buf][k + j][m] = ra[l][j];
+            } else {
+                const int k = f / (BM / 4), m = (f % (BM / 4)) * 4;
+                *reinterpret_cast<float4*>(&As[buf][k][m]) = make_float4(ra[l][0], ra[l][1], ra[l][2], ra[l][3]);
+            }
+        }
+#pragma unroll
+        for (int l = 0; l < LB; ++l) {
+            const int f = tid + l * NT;
+            if (f >= B4) continue;
+            if (!TB) {
+                const int k = f / (BN / 4), n = (f % (BN / 4)) * 4;
+                *reinterpret_cast<float4*>(&Bs[buf][k][n]) = make_float4(rb[l][0], rb[l][1], rb[l][2], rb[l][3]);
+            } else {
+                const int n = f / (BK / 4), k = (f % (BK / 4)) * 4;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) Bs[buf][k + j][n] = rb[l][j];
+            }
+        }
+    };
+
+    float acc[4 * RM][4 * RN];
+#pragma unroll
+    for (int i = 0; i < 4 * RM; ++i)
+#pragma unroll
+        for (int j = 0; j < 4 * RN; ++j) acc[i][j] = 0.0f;
+
+    const int nk = (p.K + BK - 1) / BK;
+    if (nk > 0) {
+        fetch(0);
+        stash(0);
+    }
+    __syncthreads();
+    for (int t = 0; t < nk; ++t) {
+        const int buf = t & 1;
+        if (t + 1 < nk) fetch((t + 1) * BK);
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            float a[4 * RM], bv[4 * RN];
+#pragma unroll
+            for (int r = 0; r < RM; ++r) {
+                const float4 v = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4 + r * (BM / RM)]);
+                a[r * 4 + 0] = v.x; a[r * 4 + 1] = v.y; a[r * 4 + 2] = v.z; a[r * 4 + 3] = v.w;
+            }
+#pragma unroll
+            for (int c = 0; c < RN; ++c) {
+                const float4 v = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4 + c * (BN / RN)]);
+                bv[c * 4 + 0] = v.x; bv[c * 4 + 1] = v.y; bv[c * 4 + 2] = v.z; bv[c * 4 + 3] = v.w;
+            }
+#pragma unroll
+            for (int i = 0; i < 4 * RM; ++i)
+#pragma unroll
+                for (int j = 0; j < 4 * RN; ++j) acc[i][j] = fmaf(a[i], bv[j], acc[i][j]);
+        }
+        if (t + 1 < nk) stash(buf ^ 1);
+        __syncthreads();
+    }
+
+    // epilogue: bias, ReLU, store
+#pragma unroll
+    for (int r = 0; r < RM; ++r) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int row = m0 + ty * 4 + r * (BM / RM) + i;
+            if (row >= p.M) continue;
+            float* crow = C + (int64_t)row * p.ldc;
+#pragma unroll
+            for (int c = 0; c < RN; ++c) {
+                const int col = n0 + tx * 4 + c * (BN / RN);
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float x = acc[r * 4 + i][c * 4 + j];
+                    if (p.bias && col + j < p.N) x += __ldg(p.bias + col + j);
+                    if (p.relu) x = fmaxf(x, 0.0f);
+                    v[j] = x;
+                }
+                if (p.vecC && col + 3 < p.N) {
+                    *reinterpret_cast<float4*>(crow + col) = make_float4(v[0], v[1], v[2], v[3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        if (col + j < p.N) crow[col + j] = v[j];
+                }
+            }
+        }
+    }
+}
+
+template <int BM, int BN, int BK, int RM, int RN>
+static void launch_cfg(const Params& p, int batch, bool TA, bool TB, cudaStream_t s) {
+    constexpr int threads = (BM / (4 * RM)) * (BN / (4 * RN));
+    dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, batch);
+    ProfScope prof(s, KID_FFMA_GEMM);
+    if (!TA && !TB) ffma_gemm_kernel<BM, BN, BK, RM, RN, false, false><<<grid, threads, 0, s>>>(p);
+    else if (!TA && TB) ffma_gemm_kernel<BM, BN, BK, RM, RN, false, true><<<grid, threads, 0, s>>>(p);
+    else if (TA && !TB) ffma_gemm_kernel<BM, BN, BK, RM, RN, true, false><<<grid, threads, 0, s>>>(p);
+    else ffma_gemm_kernel<BM, BN, BK, RM, RN, true, true><<<grid, threads, 0, s>>>(p);
+}
+
+static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+
+}  // namespace ffma
+
+int ffma_gemm_run(const GemmArgs& a, cudaStream_t s) {
+    using namespace ffma;
+    Params p;
+    p.M = a.M; p.N = a.N; p.K = a.K;
+    p.A = a.A; p.lda = a.lda; p.strideA = a.strideA;
+    p.B = a.B; p.ldb = a.ldb; p.strideB = a.strideB;
+    p.C = a.C; p.ldc = a.ldc; p.strideC = a.strideC;
+    p.bias = a.bias; p.relu = a.relu;
+    p.vecA = aligned16(a.A) && (a.lda % 4 == 0) && (a.strideA % 4 == 0);
+    p.vecB = aligned16(a.B) && (a.ldb % 4 == 0) && (a.strideB % 4 == 0);
+    p.vecC = aligned16(a.C) && (a.ldc % 4 == 0) && (a.strideC % 4 == 0);
+    if (a.batch > 65535) return set_status(JST_ERR_ARG, "ffma: batch > 65535");
+    // Large tiles once there are enough of them to fill the 148 SMs; 64 x 64
+    // tiles (4 x 4 per thread) otherwise.
+    const long long big_tiles = (long long)((a.M + 127) / 128) * ((a.N + 127) / 128) * a.batch;
+    if (big_tiles >= 148)
+        launch_cfg<128, 128, 8, 2, 2>(p, a.batch, a.transA, a.transB, s);
+    else
+        launch_cfg<64, 64, 16, 1, 1>(p, a.batch, a.transA, a.transB, s);
+    if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "ffma_gemm_kernel launch failed");
+    return JST_OK;
+}
+
+// ------------------------------------------------------------ K == 0 fill
+__global__ void fill_epilogue_kernel(float* C, int M, int N, int64_t ldc, int64_t strideC, const float* bias,
+                                     int relu) {
+    const int b = blockIdx.z;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)M * N;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / N), c = (int)(i % N);
+        float v = bias ? bias[c] : 0.0f;
+        if (relu) v = fmaxf(v, 0.0f);
+        C[(int64_t)b * strideC + (int64_t)r * ldc + c] = v;
+    }
+}
+
+int fill_epilogue_run(const GemmArgs& a, cudaStream_t s) {
+    const int64_t total = (int64_t)a.M * a.N;
+    if (total == 0) return JST_OK;
+    const int blocks = (int)((total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024);
+    ProfScope prof(s, KID_FILL);
+    fill_epilogue_kernel<<<dim3(blocks, 1, a.batch), 256, 0, s>>>(a.C, a.M, a.N, a.ldc, a.strideC, a.bias, a.relu);
+    if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "fill kernel launch failed");
+    return JST_OK;
+}
+
+}  // namespace jst

@@ -1,0 +1,59 @@
+// gemm_internal.h -- shared declarations between the kernels and the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/jstorch_gemm.h"
+
+namespace jst {
+
+// Normalised, validated GEMM request (see jst_gemm_desc for the meaning).
+struct GemmArgs {
+    int transA, transB;
+    int M, N, K, batch;
+    const float* A; int64_t lda, strideA;
+    const float* B; int64_t ldb, strideB;
+    float* C; int64_t ldc, strideC;
+    const float* bias;
+    int relu;
+};
+
+// Record `status` with `msg` as the calling thread's last status; returns status.
+int set_status(int status, const char* msg);
+
+// Per-device error word written by kernels whose bounded waits gave up.
+uint32_t* device_error_word();
+
+// 3 x TF32 tcgen05 path
+size_t tc_workspace_bytes(const GemmArgs& a);
+int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s);
+
+// FFMA SIMT path (no workspace)
+int ffma_gemm_run(const GemmArgs& a, cudaStream_t s);
+
+// K == 0: C = epilogue(0)
+int fill_epilogue_run(const GemmArgs& a, cudaStream_t s);
+
+// ---- launch accounting / optional event timing (profile.cu)
+enum KernelId { KID_TC_GEMM = 0, KID_SPLIT_ROWS, KID_SPLIT_TRANSPOSE, KID_FFMA_GEMM, KID_FILL, KERNEL_ID_COUNT };
+
+// Construct immediately before a kernel launch and let it go out of scope
+// right after: counts the launch and, when profiling is on, brackets it with
+// CUDA events on stream `s`.
+class ProfScope {
+  public:
+    ProfScope(cudaStream_t s, int kernel);
+    ~ProfScope();
+    ProfScope(const ProfScope&) = delete;
+    ProfScope& operator=(const ProfScope&) = delete;
+
+  private:
+    cudaStream_t s_;
+    int kernel_;
+    void* ev0_ = nullptr;
+    void* ev1_ = nullptr;
+};
+
+}  // namespace jst

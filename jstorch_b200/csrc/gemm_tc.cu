@@ -1,0 +1,390 @@
+// gemm_tc.cu -- split-precision (3 x TF32) fp32 GEMM on the sm_100a tensor
+// cores (tcgen05.mma kind::tf32, accumulator in TMEM, operands staged by TMA).
+//
+// Replaces the cuBLAS sgemm of native/ops/matmul.cu:35-36 / :48-49 / :61-62,
+// which runs single-pass TF32 (matmul.cu:12).  Here each fp32 operand x is
+// split into hi = rn_tf32(x) and lo = rn_tf32(x - hi), and
+//     A*B ~= A_lo*B_hi + A_hi*B_lo + A_hi*B_hi
+// is accumulated in fp32 in TMEM (the dropped A_lo*B_lo term is below 2^-22
+// relative per product), which keeps the result within the fp32 interface's
+// tolerance while running on the tensor pipe.
+//
+// Two kernels:
+//   split_*      one HBM pass over each operand: writes hi and lo planes in a
+//                K-major layout [batch][rows][Kp] (Kp = K rounded up to 4, so
+//                rows are 16-byte aligned for TMA).  This pass also absorbs
+//                the NN / NT / TN layouts: an MN-major operand is transposed
+//                through shared memory on the way.
+//   tc_gemm      warp-specialised pipeline per 128 x 256 output tile:
+//                  warp 0      TMA producer: 4 tiles (A_hi, A_lo, B_hi, B_lo)
+//                              per 16-wide k-slab, swizzle-64B, into a
+//                              4-stage shared-memory ring
+//                  warp 1      allocates 256 TMEM columns; one thread issues
+//                              6 tcgen05.mma (2 k-steps x 3 products) per slab
+//                              and commits each slab back to the producer
+//                  warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns,
+//                              fused bias / ReLU, direct stores to C
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "gemm_internal.h"
+#include "ptx.cuh"
+
+namespace jst {
+
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 16;  // fp32 elements per k-slab: 64-byte rows, swizzle-64B
+constexpr int STAGES = 4;
+constexpr int THREADS = 192;
+constexpr uint32_t TMEM_COLS = 256;
+
+constexpr uint32_t A_TILE_BYTES = BM * BK * 4;  // 8 KiB
+constexpr uint32_t B_TILE_BYTES = BN * BK * 4;  // 16 KiB
+constexpr uint32_t STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;  // 48 KiB
+constexpr uint32_t RING_BYTES = STAGES * STAGE_BYTES;                  // 192 KiB
+constexpr uint32_t SMEM_BYTES = RING_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+
+struct Params {
+    int M, N, K, batch;
+    float* C;
+    int64_t ldc, strideC;
+    const float* bias;
+    int relu;
+    int tiles_m, tiles_n;
+    uint32_t* err;  // device error word
+};
+
+__device__ __forceinline__ float epi(float v, const float* bias, int col, int relu) {
+    if (bias) v += __ldg(bias + col);
+    if (relu) v = fmaxf(v, 0.0f);
+    return v;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
+                   const __grid_constant__ CUtensorMap tm_b_hi, const __grid_constant__ CUtensorMap tm_b_lo,
+                   const Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment keeps every tile on a swizzle-pattern boundary
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + RING_BYTES);
+    uint64_t* empty_bar = full_bar + STAGES;
+    uint64_t* accum_bar = empty_bar + STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+    volatile uint32_t* err = tmem_slot + 1;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    // grouped rasterisation: 8 tile-rows share a band so concurrently running
+    // CTAs reuse the same B panels from L2
+    const int tiles_per_batch = p.tiles_m * p.tiles_n;
+    const int bidx = blockIdx.x / tiles_per_batch;
+    const int t = blockIdx.x % tiles_per_batch;
+    constexpr int GROUP = 8;
+    const int group_span = GROUP * p.tiles_n;
+    const int g = t / group_span;
+    const int first_m = g * GROUP;
+    const int gm = min(p.tiles_m - first_m, GROUP);
+    const int tm = first_m + (t % group_span) % gm;
+    const int tn = (t % group_span) / gm;
+    const int m0 = tm * BM;
+    const int n0 = tn * BN;
+    const int num_kb = (p.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(&full_bar[s], 1);
+            ptx::mbar_init(&empty_bar[s], 1);
+        }
+        ptx::mbar_init(accum_bar, 1);
+        *err = 0;
+        ptx::fence_barrier_init();
+        ptx::tma_prefetch_desc(&tm_a_hi);
+        ptx::tma_prefetch_desc(&tm_a_lo);
+        ptx::tma_prefetch_desc(&tm_b_hi);
+        ptx::tma_prefetch_desc(&tm_b_lo);
+    }
+    if (warp == 1) ptx::tmem_alloc<TMEM_COLS>(tmem_slot);
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t phase = (kb / STAGES) & 1;
+                if (!ptx::mbar_wait(&empty_bar[s], phase ^ 1, err)) break;
+                uint8_t* st = smem + s * STAGE_BYTES;
+                ptx::mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+                const int kx = kb * BK;
+                ptx::tma_load_3d(st, &tm_a_hi, &full_bar[s], kx, m0, bidx);
+                ptx::tma_load_3d(st + A_TILE_BYTES, &tm_a_lo, &full_bar[s], kx, m0, bidx);
+                ptx::tma_load_3d(st + 2 * A_TILE_BYTES, &tm_b_hi, &full_bar[s], kx, n0, bidx);
+                ptx::tma_load_3d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_b_lo, &full_bar[s], kx, n0, bidx);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN);
+            bool ok = true;
+            for (int kb = 0; kb < num_kb && ok; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t phase = (kb / STAGES) & 1;
+                if (!ptx::mbar_wait(&full_bar[s], phase, err)) { ok = false; break; }
+                ptx::tc_fence_after();
+                const uint32_t st = ptx::smem_u32(smem + s * STAGE_BYTES);
+                const uint32_t a_hi = st, a_lo = st + A_TILE_BYTES;
+                const uint32_t b_hi = st + 2 * A_TILE_BYTES, b_lo = b_hi + B_TILE_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; ++kk) {  // 8 tf32 = 32 bytes per MMA
+                    const uint32_t off = kk * 32;
+                    const uint32_t acc0 = (kb | kk) != 0;
+                    ptx::mma_tf32(tmem_base, ptx::smem_desc_kmajor(a_lo + off, 64),
+                                  ptx::smem_desc_kmajor(b_hi + off, 64), idesc, acc0);
+                    ptx::mma_tf32(tmem_base, ptx::smem_desc_kmajor(a_hi + off, 64),
+                                  ptx::smem_desc_kmajor(b_lo + off, 64), idesc, 1);
+                    ptx::mma_tf32(tmem_base, ptx::smem_desc_kmajor(a_hi + off, 64),
+                                  ptx::smem_desc_kmajor(b_hi + off, 64), idesc, 1);
+                }
+                ptx::mma_commit(&empty_bar[s]);  // slot s is free once these MMAs finish
+            }
+            ptx::mma_commit(accum_bar);  // always signalled, also on the error path
+        }
+    } else {
+        // ---------------------------------------------------- epilogue
+        // one lane waits and broadcasts, so the warp stays converged for the
+        // .sync.aligned TMEM loads below
+        int okw = 0;
+        if (lane == 0) okw = ptx::mbar_wait(accum_bar, 0, err) && *err == 0;
+        const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+        ptx::tc_fence_after();
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const int row = m0 + q * 32 + lane;
+        const bool row_ok = ok && row < p.M;
+        float* crow = p.C + (int64_t)bidx * p.strideC + (int64_t)row * p.ldc;
+        const bool vec = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                         ((p.strideC & 3) == 0);
+        if (ok) {
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                const int col0 = n0 + c * 32;
+                if (col0 >= p.N) break;  // warp-uniform
+                uint32_t r[32];
+                ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
+                ptx::tmem_ld_wait();
+                if (!row_ok) continue;
+                if (vec && col0 + 32 <= p.N) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        float4 v;
+                        v.x = epi(__uint_as_float(r[j + 0]), p.bias, col0 + j + 0, p.relu);
+                        v.y = epi(__uint_as_float(r[j + 1]), p.bias, col0 + j + 1, p.relu);
+                        v.z = epi(__uint_as_float(r[j + 2]), p.bias, col0 + j + 2, p.relu);
+                        v.w = epi(__uint_as_float(r[j + 3]), p.bias, col0 + j + 3, p.relu);
+                        *reinterpret_cast<float4*>(crow + col0 + j) = v;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (col0 + j < p.N) crow[col0 + j] = epi(__uint_as_float(r[j]), p.bias, col0 + j, p.relu);
+                }
+            }
+        }
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc<TMEM_COLS>(tmem_base);
+    }
+    if (threadIdx.x == 0 && *err != 0) atomicOr(p.err, *err);
+}
+
+// --------------------------------------------------------------- split passes
+// Source K-major: element (b, r, k) at src[b*sstride + r*ld + k].
+template <bool VEC>
+__global__ void split_rows_kernel(const float* __restrict__ src, int64_t ld, int64_t sstride, int rows, int K,
+                                  int Kp, int batch, float* __restrict__ hi, float* __restrict__ lo) {
+    const int kq = Kp >> 2;  // float4 groups per output row
+    const int64_t total = (int64_t)batch * rows * kq;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t rr = i / kq;  // b * rows + r
+        const int k = (int)(i - rr * kq) * 4;
+        const int b = (int)(rr / rows);
+        const int r = (int)(rr - (int64_t)b * rows);
+        const float* s = src + b * sstride + r * ld;
+        float v[4];
+        if (VEC && k + 3 < K) {
+            const float4 x = __ldg(reinterpret_cast<const float4*>(s + k));
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? __ldg(s + k + j) : 0.0f;
+        }
+        float h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            h[j] = ptx::to_tf32(v[j]);
+            l[j] = ptx::to_tf32(v[j] - h[j]);
+        }
+        const int64_t o = rr * Kp + k;
+        *reinterpret_cast<float4*>(hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4*>(lo + o) = make_float4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+// Source MN-major: element (b, r, k) at src[b*sstride + k*ld + r]; transposed
+// through a 32 x 32 shared tile so both the read and the write are coalesced.
+__global__ void split_transpose_kernel(const float* __restrict__ src, int64_t ld, int64_t sstride, int rows,
+                                       int K, int Kp, float* __restrict__ hi, float* __restrict__ lo) {
+    __shared__ float tile[32][33];
+    const int b = blockIdx.z;
+    const int r0 = blockIdx.x * 32;
+    const int k0 = blockIdx.y * 32;
+    const float* s = src + b * sstride;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+        const int k = k0 + threadIdx.y + j;
+        const int r = r0 + threadIdx.x;
+        tile[threadIdx.y + j][threadIdx.x] = (k < K && r < rows) ? __ldg(s + (int64_t)k * ld + r) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+        const int r = r0 + threadIdx.y + j;
+        const int k = k0 + threadIdx.x;
+        if (r < rows && k < Kp) {
+            const float v = tile[threadIdx.x][threadIdx.y + j];
+            const float h = ptx::to_tf32(v);
+            const int64_t o = ((int64_t)b * rows + r) * Kp + k;
+            hi[o] = h;
+            lo[o] = ptx::to_tf32(v - h);
+        }
+    }
+}
+
+// --------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 3-D map over a K-major plane [batch][rows][Kp] with box {BK, box_rows, 1}.
+static bool make_plane_map(CUtensorMap* m, const float* base, int K, int rows, int batch, int Kp, int box_rows) {
+    auto enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
+    cuuint64_t strides[2] = {(cuuint64_t)Kp * 4, (cuuint64_t)Kp * 4 * (cuuint64_t)rows};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+static int launch_split(const float* src, bool kmajor, int64_t ld, int64_t sstride, int rows, int K, int Kp,
+                        int batch, float* hi, float* lo, cudaStream_t s) {
+    if (rows == 0 || Kp == 0) return JST_OK;
+    if (kmajor) {
+        const bool vec = ((ld & 3) == 0) && ((sstride & 3) == 0) && ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+        const int64_t total = (int64_t)batch * rows * (Kp / 4);
+        const int threads = 256;
+        const int64_t want = (total + threads - 1) / threads;
+        const int blocks = (int)(want < 148 * 16 ? want : 148 * 16);
+        ProfScope prof(s, KID_SPLIT_ROWS);
+        if (vec)
+            split_rows_kernel<true><<<blocks, threads, 0, s>>>(src, ld, sstride, rows, K, Kp, batch, hi, lo);
+        else
+            split_rows_kernel<false><<<blocks, threads, 0, s>>>(src, ld, sstride, rows, K, Kp, batch, hi, lo);
+    } else {
+        dim3 grid((rows + 31) / 32, (Kp + 31) / 32, batch);
+        ProfScope prof(s, KID_SPLIT_TRANSPOSE);
+        split_transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(src, ld, sstride, rows, K, Kp, hi, lo);
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? JST_OK : JST_ERR_CUDA;
+}
+
+}  // namespace tc
+
+size_t tc_workspace_bytes(const GemmArgs& a) {
+    const size_t Kp = (size_t)((a.K + 3) & ~3);
+    return 2 * Kp * ((size_t)a.M + (size_t)a.N) * (size_t)a.batch * sizeof(float);
+}
+
+int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {
+    using namespace tc;
+    const int Kp = (a.K + 3) & ~3;
+    float* ws = static_cast<float*>(workspace);
+    const size_t a_plane = (size_t)a.batch * a.M * Kp;
+    const size_t b_plane = (size_t)a.batch * a.N * Kp;
+    float* a_hi = ws;
+    float* a_lo = a_hi + a_plane;
+    float* b_hi = a_lo + a_plane;
+    float* b_lo = b_hi + b_plane;
+
+    // op(A) rows are M: K-major unless A is stored transposed.
+    int rc = launch_split(a.A, !a.transA, a.lda, a.strideA, a.M, a.K, Kp, a.batch, a_hi, a_lo, s);
+    if (rc) return set_status(rc, "split of A failed to launch");
+    // op(B)^T rows are N: K-major when B is stored [N, K] (transB).
+    rc = launch_split(a.B, a.transB, a.ldb, a.strideB, a.N, a.K, Kp, a.batch, b_hi, b_lo, s);
+    if (rc) return set_status(rc, "split of B failed to launch");
+
+    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+    if (!make_plane_map(&m_ahi, a_hi, a.K, a.M, a.batch, Kp, BM) ||
+        !make_plane_map(&m_alo, a_lo, a.K, a.M, a.batch, Kp, BM) ||
+        !make_plane_map(&m_bhi, b_hi, a.K, a.N, a.batch, Kp, BN) ||
+        !make_plane_map(&m_blo, b_lo, a.K, a.N, a.batch, Kp, BN))
+        return set_status(JST_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+            cudaSuccess)
+            return set_status(JST_ERR_CUDA, "cudaFuncSetAttribute(tc_gemm_kernel) failed");
+        attr_set[dev] = true;
+    }
+    Params p;
+    p.M = a.M; p.N = a.N; p.K = a.K; p.batch = a.batch;
+    p.C = a.C; p.ldc = a.ldc; p.strideC = a.strideC;
+    p.bias = a.bias; p.relu = a.relu;
+    p.tiles_m = (a.M + BM - 1) / BM;
+    p.tiles_n = (a.N + BN - 1) / BN;
+    p.err = device_error_word();
+    const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * a.batch;
+    if (grid > 0x7fffffff) return set_status(JST_ERR_ARG, "tc: too many tiles");
+    {
+        ProfScope prof(s, KID_TC_GEMM);
+        tc_gemm_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, s>>>(m_ahi, m_alo, m_bhi, m_blo, p);
+    }
+    if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "tc_gemm_kernel launch failed");
+    return JST_OK;
+}
+
+}  // namespace jst

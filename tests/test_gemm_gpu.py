@@ -1,0 +1,194 @@
+"""Parity of the sm_100a GEMM kernels with the fp64 oracle, through the C ABI.
+
+Tolerance (the path's stated bound): for every checked element
+    |C - C_ref| / (||op(A)_i,:|| * ||op(B)_:,j|| + |bias_j|) <= 2e-6
+with C_ref the fp64-accumulated product of the same fp32 inputs.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+
+TOL = 2e-6
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(x):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def _check(A, B, C, *, ta=False, tb=False, bias=None, relu=False, rows=None, tol=TOL):
+    ref = oracle.gemm_f64(A, B, transA=ta, transB=tb, bias=bias, relu=relu, rows=rows)
+    err, where = oracle.max_rel_err(A, B, C, ref, transA=ta, transB=tb, bias=bias, rows=rows)
+    assert err <= tol, f"max rel err {err:.3e} at {where}"
+    return err
+
+
+def _rand(rng, *shape, dist="normal"):
+    if dist == "uniform":
+        return (rng.random(shape, dtype=np.float32) * 2 - 1).astype(np.float32)
+    return rng.standard_normal(shape, dtype=np.float32)
+
+
+@pytest.fixture(scope="module")
+def jst():
+    import jstorch_b200
+    jstorch_b200.load()
+    return jstorch_b200
+
+
+KERNELS = ["ffma", "tc3xtf32"]
+
+
+def test_readme_known_answer_through_host_matmul(jst):
+    # README.md:41-55: torch.matmul(a, b, 2, 3, 4) -> [38, 44, 50, 56, 83, 98, 113, 128]
+    a = np.array([1, 2, 3, 4, 5, 6], np.float32)
+    b = np.arange(1, 13, dtype=np.float32)
+    c = jst.torch.matmul(a, b, 2, 3, 4)
+    assert c.dtype == np.float32 and c.tolist() == [38, 44, 50, 56, 83, 98, 113, 128]
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_readme_known_answer_each_kernel(jst, kernel):
+    a = _dev(np.array([[1, 2, 3], [4, 5, 6]], np.float32))
+    b = _dev(np.arange(1, 13, dtype=np.float32).reshape(3, 4))
+    c = jst.gemm(a, b, kernel=kernel).cpu().numpy()
+    assert c.tolist() == [[38, 44, 50, 56], [83, 98, 113, 128]]
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (3, 17, 31), (33, 127, 129), (128, 256, 64), (129, 257, 65),
+                                   (200, 300, 1000), (512, 512, 512)])
+def test_layouts_odd_shapes(jst, kernel, ta, tb, M, N, K):
+    rng = np.random.default_rng(M * 131 + N * 7 + K + 1000 * ta + 2000 * tb)
+    A = _rand(rng, K, M) if ta else _rand(rng, M, K)
+    B = _rand(rng, N, K) if tb else _rand(rng, K, N)
+    a, b = _dev(A), _dev(B)
+    av = a.t() if ta else a  # transposed views reach the kernels as TN / NT operands
+    bv = b.t() if tb else b
+    C = jst.gemm(av, bv, kernel=kernel).cpu().numpy()
+    _check(A, B, C, ta=bool(ta), tb=bool(tb))
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("relu", [False, True])
+def test_bias_relu_epilogue(jst, kernel, relu):
+    rng = np.random.default_rng(5)
+    X, W, b = _rand(rng, 300, 200), _rand(rng, 130, 200), _rand(rng, 130)
+    C = jst.gemm(_dev(X), _dev(W).t(), bias=_dev(b), relu=relu, kernel=kernel).cpu().numpy()
+    _check(X, W, C, tb=True, bias=b, relu=relu)
+    if relu:
+        assert (C >= 0).all()
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_strided_batched(jst, kernel):
+    rng = np.random.default_rng(9)
+    A, B = _rand(rng, 5, 70, 40), _rand(rng, 5, 40, 90)
+    C = jst.gemm(_dev(A), _dev(B), kernel=kernel).cpu().numpy()
+    _check(A, B, C)
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_leading_dimension_and_unaligned_views(jst, kernel):
+    import torch
+    rng = np.random.default_rng(11)
+    big = _rand(rng, 100, 75)          # ld 75: not a multiple of 4
+    A = big[3:90, 1:70]                # unaligned base, ld 75
+    B = _rand(rng, 69, 50)
+    a = _dev(big)[3:90, 1:70]
+    C = jst.gemm(a, _dev(B), kernel=kernel).cpu().numpy()
+    _check(np.ascontiguousarray(A), B, C)
+    assert a.stride() == (75, 1)
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_k_zero_and_empty(jst, kernel):
+    import torch
+    a = torch.empty((4, 0), device="cuda")
+    b = torch.empty((0, 6), device="cuda")
+    bias = _dev(np.arange(6, dtype=np.float32) - 2)
+    c = jst.gemm(a, b, bias=bias, relu=True, kernel=kernel).cpu().numpy()
+    assert c.tolist() == [[0, 0, 0, 1, 2, 3]] * 4
+    e = jst.gemm(torch.empty((0, 5), device="cuda"), torch.zeros((5, 3), device="cuda"), kernel=kernel)
+    assert e.shape == (0, 3)
+
+
+def test_reference_launchers(jst):
+    """launch_matmul / launch_bmm / launch_linear keep the reference signatures
+    (native/ops/matmul.cu:28,40,54) and results."""
+    import torch
+    lib = jst.load()
+    rng = np.random.default_rng(3)
+    A, B = _rand(rng, 96, 80), _rand(rng, 80, 112)
+    a, b = _dev(A), _dev(B)
+    c = torch.empty((96, 112), device="cuda")
+    lib.launch_matmul(a.data_ptr(), b.data_ptr(), c.data_ptr(), 96, 80, 112, None)
+    assert lib.jst_get_last_status() == 0
+    _check(A, B, c.cpu().numpy())
+
+    A3, B3 = _rand(rng, 4, 33, 20), _rand(rng, 4, 20, 45)
+    c3 = torch.empty((4, 33, 45), device="cuda")
+    lib.launch_bmm(_dev(A3).data_ptr(), _dev(B3).data_ptr(), c3.data_ptr(), 4, 33, 20, 45, None)
+    assert lib.jst_get_last_status() == 0
+    _check(A3, B3, c3.cpu().numpy())
+
+    X, W, bias = _rand(rng, 256, 784), _rand(rng, 1024, 784), _rand(rng, 1024)
+    y = torch.empty((256, 1024), device="cuda")
+    x_d, w_d, b_d = _dev(X), _dev(W), _dev(bias)
+    lib.launch_linear(x_d.data_ptr(), w_d.data_ptr(), b_d.data_ptr(), y.data_ptr(), 256, 784, 1024, None)
+    assert lib.jst_get_last_status() == 0
+    _check(X, W, y.cpu().numpy(), tb=True, bias=bias)
+    lib.launch_linear(x_d.data_ptr(), w_d.data_ptr(), None, y.data_ptr(), 256, 784, 1024, None)
+    _check(X, W, y.cpu().numpy(), tb=True)
+    assert jst.device_error() == 0
+
+
+def test_host_matmul_config1(jst):
+    """Config 1: 512^3 through torch.matmul(a, b, 512, 512, 512) on host arrays."""
+    from jstorch_b200 import synth
+    A, B = synth.config1()
+    C = jst.torch.matmul(A.reshape(-1), B.reshape(-1), 512, 512, 512).reshape(512, 512)
+    _check(A, B, C)
+
+
+def test_config3_sampled_rows(jst):
+    """Config 3 (8192^3, N(0,1)): both kernels, 96 sampled rows x all columns."""
+    import torch
+    from jstorch_b200 import synth
+    A, B = synth.config3()
+    a, b = _dev(A), _dev(B)
+    rows = np.sort(np.random.default_rng(0).choice(8192, 96, replace=False)).astype(np.int32)
+    rows[0], rows[-1] = 0, 8191
+    ref = oracle.gemm_f64(A, B, rows=rows)
+    for kernel in KERNELS:
+        c = jst.gemm(a, b, kernel=kernel)
+        C = c[torch.from_numpy(rows).long().cuda()].cpu().numpy()
+        full = np.zeros((8192, 8192), np.float32)
+        full[rows] = C
+        err, where = oracle.max_rel_err(A, B, full, ref, rows=rows)
+        assert err <= TOL, (kernel, err, where)
+        del c
+    assert jst.device_error() == 0
+
+
+def test_config4_batched_attention_shapes(jst):
+    from jstorch_b200 import synth
+    q, kt, p, v = synth.config4()
+    for kernel in KERNELS:
+        s = jst.gemm(_dev(q), _dev(kt), kernel=kernel).cpu().numpy()
+        _check(q, kt, s)
+        o = jst.gemm(_dev(p), _dev(v), kernel=kernel).cpu().numpy()
+        _check(p, v, o)
+
+
+def test_kernel_choice_heuristic(jst):
+    assert jst.select_kernel(8192, 8192, 8192) == "tc3xtf32"
+    assert jst.select_kernel(256, 10, 1024) == "ffma"
+    assert jst.select_kernel(2, 4, 3) == "ffma"
