@@ -205,7 +205,8 @@ def run_jstorch(args) -> None:
     a = torch.from_numpy(A).to(dev)
     b = torch.from_numpy(B).to(dev)
     c = torch.empty((M, N), dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)  # every library call below runs on this stream
     flops = 2.0 * M * N * K
 
     # ---- device-resident timing (value) + live kernel timing (roofline)

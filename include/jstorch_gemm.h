@@ -115,7 +115,7 @@ int jst_matmul_host(const float* a, const float* b, float* c, int M, int K, int 
 /*
  * Stream-ordered form of jst_matmul_host (no counterpart in the reference):
  * enqueues the host->device copies, the GEMM and the device->host copy on
- * `stream` and returns.  With pinned (page-locked) host buffers the call is
+ * `stream` (NULL = the legacy default stream) and returns.  With pinned (page-locked) host buffers the call is
  * asynchronous and `c` is valid once the stream reaches that point; with
  * pageable buffers the copies synchronise as cudaMemcpyAsync does.  The
  * device staging buffers are per device: calls on different streams of the

@@ -177,9 +177,11 @@ struct HostStage {
 static HostStage g_host[64];
 
 // Host-array GEMM: stage a and b to device buffers cached per device, run the
-// GEMM, copy C back.  `stream` == nullptr uses the library's own stream and
-// waits for completion; otherwise everything is enqueued on `stream`.
-static int host_matmul(const float* a, const float* b, float* c, int M, int K, int N, cudaStream_t user_stream) {
+// GEMM, copy C back.  sync: on the library's own stream, waiting for the
+// result; otherwise everything is enqueued on `user_stream` (0 = the legacy
+// default stream) and the call returns.
+static int host_matmul(const float* a, const float* b, float* c, int M, int K, int N, cudaStream_t user_stream,
+                       bool sync) {
     if (M < 0 || K < 0 || N < 0) return set_status(JST_ERR_ARG, "negative dimension");
     if ((M > 0 && K > 0 && !a) || (K > 0 && N > 0 && !b) || (M > 0 && N > 0 && !c))
         return set_status(JST_ERR_ARG, "null host pointer");
@@ -188,11 +190,11 @@ static int host_matmul(const float* a, const float* b, float* c, int M, int K, i
     if (rc) return rc;
     HostStage& h = g_host[dev];
     std::lock_guard<std::mutex> lk(h.mu);
-    if (!user_stream && !h.stream) {
+    if (sync && !h.stream) {
         rc = cuda_status(cudaStreamCreateWithFlags(&h.stream, cudaStreamNonBlocking), "stream create");
         if (rc) return rc;
     }
-    cudaStream_t st = user_stream ? user_stream : h.stream;
+    cudaStream_t st = sync ? h.stream : user_stream;
     const size_t na = (size_t)M * K, nb = (size_t)K * N, nc = (size_t)M * N;
     // keep each plane 16-byte aligned inside the staging buffer
     auto up4 = [](size_t n) { return (n + 3) & ~size_t(3); };
@@ -228,7 +230,7 @@ static int host_matmul(const float* a, const float* b, float* c, int M, int K, i
         rc = cuda_status(cudaMemcpyAsync(c, dC, nc * sizeof(float), cudaMemcpyDeviceToHost, st), "D2H C");
         if (rc) return rc;
     }
-    if (user_stream) return set_status(JST_OK, nullptr);
+    if (!sync) return set_status(JST_OK, nullptr);
     rc = cuda_status(cudaStreamSynchronize(st), "matmul synchronise");
     if (rc) return rc;
     uint32_t* w = g_dev[dev].err_word;
@@ -302,12 +304,11 @@ void launch_linear(const float* x, const float* w, const float* bias, float* out
 }
 
 int jst_matmul_host(const float* a, const float* b, float* c, int M, int K, int N) {
-    return jst::host_matmul(a, b, c, M, K, N, nullptr);
+    return jst::host_matmul(a, b, c, M, K, N, nullptr, true);
 }
 
 int jst_matmul_host_async(const float* a, const float* b, float* c, int M, int K, int N, jst_stream_t stream) {
-    if (!stream) return jst::set_status(JST_ERR_ARG, "jst_matmul_host_async needs a stream");
-    return jst::host_matmul(a, b, c, M, K, N, reinterpret_cast<cudaStream_t>(stream));
+    return jst::host_matmul(a, b, c, M, K, N, reinterpret_cast<cudaStream_t>(stream), false);
 }
 
 int jst_device_error(void) {

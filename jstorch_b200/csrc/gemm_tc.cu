@@ -19,9 +19,10 @@
 //                  warp 0      TMA producer: 4 tiles (A_hi, A_lo, B_hi, B_lo)
 //                              per 16-wide k-slab, swizzle-64B, into a
 //                              4-stage shared-memory ring
-//                  warp 1      allocates 256 TMEM columns; one thread issues
-//                              6 tcgen05.mma (2 k-steps x 3 products) per slab
-//                              and commits each slab back to the producer
+//                  warp 1      allocates 512 TMEM columns (two accumulators);
+//                              one thread issues 6 tcgen05.mma (2 k-steps x 3
+//                              products) per slab and commits each slab back to
+//                              the producer
 //                  warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns,
 //                              fused bias / ReLU, direct stores to C
 #include <cuda.h>
@@ -44,7 +45,14 @@ constexpr int BN = 256;
 constexpr int BK = 16;  // fp32 elements per k-slab: 64-byte rows, swizzle-64B
 constexpr int STAGES = 4;
 constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 256;
+// Two fp32 accumulators of 128 lanes x 256 columns: D_hi receives only the
+// A_hi*B_hi products, D_lo the two small cross products.  The tensor core's
+// fp32 accumulation truncates each add relative to the accumulator's own
+// magnitude, so keeping the ~2^-11 smaller cross terms out of D_hi cuts the
+// number of truncating adds into the large accumulator by three.
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t D_HI_COL = 0;
+constexpr uint32_t D_LO_COL = 256;
 
 constexpr uint32_t A_TILE_BYTES = BM * BK * 4;  // 8 KiB
 constexpr uint32_t B_TILE_BYTES = BN * BK * 4;  // 16 KiB
@@ -152,12 +160,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int kk = 0; kk < BK / 8; ++kk) {  // 8 tf32 = 32 bytes per MMA
                     const uint32_t off = kk * 32;
                     const uint32_t acc0 = (kb | kk) != 0;
-                    ptx::mma_tf32(tmem_base, ptx::smem_desc_kmajor(a_lo + off, 64),
-                                  ptx::smem_desc_kmajor(b_hi + off, 64), idesc, acc0);
-                    ptx::mma_tf32(tmem_base, ptx::smem_desc_kmajor(a_hi + off, 64),
-                                  ptx::smem_desc_kmajor(b_lo + off, 64), idesc, 1);
-                    ptx::mma_tf32(tmem_base, ptx::smem_desc_kmajor(a_hi + off, 64),
-                                  ptx::smem_desc_kmajor(b_hi + off, 64), idesc, 1);
+                    const uint64_t dah = ptx::smem_desc_kmajor(a_hi + off, 64);
+                    const uint64_t dbh = ptx::smem_desc_kmajor(b_hi + off, 64);
+                    ptx::mma_tf32(tmem_base + D_LO_COL, ptx::smem_desc_kmajor(a_lo + off, 64), dbh, idesc, acc0);
+                    ptx::mma_tf32(tmem_base + D_LO_COL, dah, ptx::smem_desc_kmajor(b_lo + off, 64), idesc, 1);
+                    ptx::mma_tf32(tmem_base + D_HI_COL, dah, dbh, idesc, acc0);
                 }
                 ptx::mma_commit(&empty_bar[s]);  // slot s is free once these MMAs finish
             }
@@ -182,10 +189,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int c = 0; c < BN / 32; ++c) {
                 const int col0 = n0 + c * 32;
                 if (col0 >= p.N) break;  // warp-uniform
-                uint32_t r[32];
-                ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
+                uint32_t r[32], rl[32];
+                const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32);
+                ptx::tmem_ld_32x32b_x32(taddr + D_HI_COL, r);
+                ptx::tmem_ld_32x32b_x32(taddr + D_LO_COL, rl);
                 ptx::tmem_ld_wait();
                 if (!row_ok) continue;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(rl[j]));
                 if (vec && col0 + 32 <= p.N) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {

@@ -134,8 +134,9 @@ def test_reference_launchers(jst):
     _check(A, B, c.cpu().numpy())
 
     A3, B3 = _rand(rng, 4, 33, 20), _rand(rng, 4, 20, 45)
+    a3, b3 = _dev(A3), _dev(B3)  # keep the device tensors alive across the async launch
     c3 = torch.empty((4, 33, 45), device="cuda")
-    lib.launch_bmm(_dev(A3).data_ptr(), _dev(B3).data_ptr(), c3.data_ptr(), 4, 33, 20, 45, None)
+    lib.launch_bmm(a3.data_ptr(), b3.data_ptr(), c3.data_ptr(), 4, 33, 20, 45, None)
     assert lib.jst_get_last_status() == 0
     _check(A3, B3, c3.cpu().numpy())
 
