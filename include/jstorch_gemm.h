@@ -93,6 +93,29 @@ int jst_gemm_ex(const jst_gemm_desc* d);
 /* Which kernel JST_KERNEL_AUTO would run for `d` (JST_KERNEL_TC3XTF32 or _FFMA). */
 int jst_gemm_select_kernel(const jst_gemm_desc* d);
 
+/*
+ * jst_gemm_tc_noalloc -- the tensor-core (3 x TF32) GEMM of jst_gemm_ex
+ * without any device allocation.  No counterpart in the reference.
+ *
+ * For callers that must not allocate device memory: code running while a
+ * CUDA graph is being captured, hosts whose device memory belongs to another
+ * allocator, and embedders that budget all device memory up front.
+ * jst_gemm_ex takes its scratch (the hi/lo split planes) from a pool it
+ * allocates; this entry point uses a fixed 64 MiB file-scope device array
+ * instead, and calls no cudaMalloc, cudaFree or other allocating routine.
+ *   - Same descriptor and result as jst_gemm_ex with kernel = TC3XTF32
+ *     (`kernel` must be AUTO or TC3XTF32).  The caller passes A, B, C, bias.
+ *   - Limit: 2 * Kp * (M + N) * batch * 4 bytes <= 64 MiB, Kp = K rounded up
+ *     to a multiple of 4 (e.g. 2048^3 fits); larger requests return
+ *     JST_ERR_ARG without launching.
+ *   - The array exists once per device, for the life of the process, and is
+ *     shared by all calls: calls whose work overlaps on the GPU (different
+ *     streams or threads) race and must be serialised by the caller.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ */
+int jst_gemm_tc_noalloc(const jst_gemm_desc* d);
+
 /* ------------------------------------------- reference-compatible launchers */
 /* native/ops/matmul.cu:28 -- row-major [M,K] x [K,N] -> [M,N] */
 void launch_matmul(const float* a, const float* b, float* c, int M, int K, int N, jst_stream_t s);

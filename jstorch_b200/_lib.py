@@ -72,6 +72,8 @@ def load() -> ctypes.CDLL:
     lib.jst_gemm_ex.argtypes = [ctypes.POINTER(GemmDesc)]
     lib.jst_gemm_select_kernel.restype = ci
     lib.jst_gemm_select_kernel.argtypes = [ctypes.POINTER(GemmDesc)]
+    lib.jst_gemm_tc_noalloc.restype = ci
+    lib.jst_gemm_tc_noalloc.argtypes = [ctypes.POINTER(GemmDesc)]
     lib.launch_matmul.restype = None
     lib.launch_matmul.argtypes = [vp, vp, vp, ci, ci, ci, vp]
     lib.launch_bmm.restype = None

@@ -136,6 +136,8 @@ static int validate(const jst_gemm_desc* d, GemmArgs* a) {
     return JST_OK;
 }
 
+int validate_gemm_desc(const jst_gemm_desc* d, GemmArgs* a) { return validate(d, a); }
+
 static int gemm(const jst_gemm_desc* d) {
     GemmArgs a;
     int rc = validate(d, &a);

@@ -20,6 +20,9 @@ struct GemmArgs {
     int relu;
 };
 
+// Check a public descriptor and normalise it into `a` (no device work).
+int validate_gemm_desc(const jst_gemm_desc* d, GemmArgs* a);
+
 // Record `status` with `msg` as the calling thread's last status; returns status.
 int set_status(int status, const char* msg);
 

@@ -347,7 +347,9 @@ size_t tc_workspace_bytes(const GemmArgs& a) {
     return 2 * Kp * ((size_t)a.M + (size_t)a.N) * (size_t)a.batch * sizeof(float);
 }
 
-int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {
+// Split both operands into `workspace` and run the tensor-core kernel;
+// `err` receives the kernel's timeout flag.
+static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cudaStream_t s) {
     using namespace tc;
     const int Kp = (a.K + 3) & ~3;
     float* ws = static_cast<float*>(workspace);
@@ -387,7 +389,7 @@ int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {
     p.bias = a.bias; p.relu = a.relu;
     p.tiles_m = (a.M + BM - 1) / BM;
     p.tiles_n = (a.N + BN - 1) / BN;
-    p.err = device_error_word();
+    p.err = err;
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * a.batch;
     if (grid > 0x7fffffff) return set_status(JST_ERR_ARG, "tc: too many tiles");
     {
@@ -398,4 +400,112 @@ int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {
     return JST_OK;
 }
 
+int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {
+    return tc_gemm_launch(a, workspace, device_error_word(), s);
+}
+
+// ----------------------------------------------------------------------------
+// Allocation-free variant (jst_gemm_tc_noalloc).
+//
+// Some callers cannot call cudaMalloc at all: code running while a CUDA graph
+// is being captured (an allocation there is either illegal or baked into the
+// graph), processes whose device memory is owned by another allocator that
+// forbids side allocations, and embedders that must size all device memory up
+// front.  For them the split planes of the 3xTF32 kernel live in this fixed,
+// file-scope device array instead of a workspace from the library's pool.
+//
+// The array is NOALLOC_SCRATCH_BYTES (64 MiB) and belongs to this module: the
+// CUDA runtime reserves it on a device when the module is loaded there (on
+// first use with lazy module loading, which is the default; at context
+// creation with CUDA_MODULE_LOADING=EAGER), and it is held until the process
+// exits.  A request whose split planes, 2 * Kp * (M + N) * batch floats with
+// Kp = K rounded up to 4, exceed it is rejected with JST_ERR_ARG.
+//
+// The array is shared by every call on a device and keeps the previous call's
+// planes.  Nothing in it has to start at zero: the split kernels rewrite every
+// row and every padded column of the planes a call uses before the GEMM reads
+// them.  The kernel's timeout word is also file-scope; each call zeroes it on
+// its stream before launching.  Two calls whose work overlaps on the GPU (on
+// different streams, or from different threads) race on the array and give
+// wrong results: serialise them.
+// ----------------------------------------------------------------------------
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(64) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_SCRATCH_BYTES / sizeof(float)];
+static __device__ __align__(256) uint32_t g_noalloc_err;
+
+namespace {
+struct NoAllocDevice {
+    bool ready = false;
+    float* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+    uint32_t* err = nullptr;   // device address of g_noalloc_err on this device
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[64];
+
+// Once per device, with that device current: resolve the device addresses of
+// the file-scope arrays.  Their host-side names are only stand-ins and must
+// never be passed to a kernel.
+int noalloc_setup(int dev, NoAllocDevice** out) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocDevice& d = g_noalloc_dev[dev];
+    if (!d.ready) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return set_status(JST_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed");
+        }
+        d.scratch = static_cast<float*>(p);
+        e = cudaGetSymbolAddress(&p, g_noalloc_err);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return set_status(JST_ERR_CUDA, "cudaGetSymbolAddress(error word) failed");
+        }
+        d.err = static_cast<uint32_t*>(p);
+        d.ready = true;
+    }
+    *out = &d;
+    return JST_OK;
+}
+}  // namespace
+
 }  // namespace jst
+
+extern "C" int jst_gemm_tc_noalloc(const jst_gemm_desc* d) {
+    using namespace jst;
+    GemmArgs a{};
+    int rc = validate_gemm_desc(d, &a);
+    if (rc) return rc;
+    if (d->kernel != JST_KERNEL_AUTO && d->kernel != JST_KERNEL_TC3XTF32)
+        return set_status(JST_ERR_ARG, "jst_gemm_tc_noalloc runs the tensor-core kernel only");
+    int dev = -1, major = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 ||
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return set_status(JST_ERR_NO_DEVICE, "no CUDA device available");
+    }
+    if (major != 10) return set_status(JST_ERR_NO_DEVICE, "libjstorch_gemm is built for sm_100a (B200) only");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(d->stream);
+    if (a.M == 0 || a.N == 0) return set_status(JST_OK, nullptr);
+    if (a.K == 0) {
+        rc = fill_epilogue_run(a, s);
+        return rc ? rc : set_status(JST_OK, nullptr);
+    }
+    const size_t need = tc_workspace_bytes(a);
+    if (need > NOALLOC_SCRATCH_BYTES) {
+        char msg[160];
+        std::snprintf(msg, sizeof(msg),
+                      "jst_gemm_tc_noalloc: split planes need %zu bytes, above the fixed %zu-byte scratch", need,
+                      NOALLOC_SCRATCH_BYTES);
+        return set_status(JST_ERR_ARG, msg);
+    }
+    NoAllocDevice* nd = nullptr;
+    rc = noalloc_setup(dev, &nd);
+    if (rc) return rc;
+    if (cudaMemsetAsync(nd->err, 0, sizeof(uint32_t), s) != cudaSuccess) {
+        cudaGetLastError();
+        return set_status(JST_ERR_CUDA, "clearing the scratch error word failed");
+    }
+    rc = tc_gemm_launch(a, nd->scratch, nd->err, s);
+    return rc ? rc : set_status(JST_OK, nullptr);
+}

@@ -1,0 +1,94 @@
+"""jst_gemm_tc_noalloc: the tensor-core GEMM for callers that cannot allocate
+device memory (graph capture, foreign allocators, fixed memory budgets).  It
+keeps its scratch in a fixed 64 MiB device array instead of allocating.
+
+Checked through the C ABI against jst_gemm_ex (the allocating entry point,
+tensor-core kernel forced) on two calls in a row with different shapes and
+inputs, so the second call runs on scratch the first one left behind.  This
+file is collected last on purpose; it also passes when run on its own.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from jstorch_b200 import _lib
+from oracle import oracle
+
+TOL = 2e-6  # the bound every GEMM test in this suite uses
+
+pytestmark = pytest.mark.gpu
+
+
+def _desc(a, b, c, M, N, K, *, transB=False, bias=None, relu=False, batch=1, stream=0):
+    d = _lib.GemmDesc()
+    d.transA, d.transB = 0, int(transB)
+    d.M, d.N, d.K = M, N, K
+    d.A, d.lda, d.strideA = a.data_ptr(), K, M * K
+    d.B, d.ldb, d.strideB = b.data_ptr(), (K if transB else N), N * K
+    d.C, d.ldc, d.strideC = c.data_ptr(), N, M * N
+    d.batch = batch
+    d.bias = bias.data_ptr() if bias is not None else None
+    d.epilogue = (_lib.EPI_BIAS if bias is not None else 0) | (_lib.EPI_RELU if relu else 0)
+    d.kernel = _lib.KERNEL_TC3XTF32
+    d.stream = stream
+    return d
+
+
+def _run_pair(M, N, K, seed, *, transB=False, with_bias=False, relu=False, batch=1):
+    import torch
+    lib = _lib.load()
+    rng = np.random.default_rng(seed)
+    shape_a = (batch, M, K) if batch > 1 else (M, K)
+    shape_b = ((batch,) if batch > 1 else ()) + ((N, K) if transB else (K, N))
+    A = rng.standard_normal(shape_a, dtype=np.float32)
+    B = rng.standard_normal(shape_b, dtype=np.float32)
+    bias_h = rng.standard_normal(N, dtype=np.float32) if with_bias else None
+    a, b = torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda()
+    bias = torch.from_numpy(bias_h).cuda() if with_bias else None
+    c_free = torch.full((batch, M, N), float("nan"), device="cuda")
+    c_ref = torch.full((batch, M, N), float("nan"), device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    d = _desc(a, b, c_free, M, N, K, transB=transB, bias=bias, relu=relu, batch=batch, stream=stream)
+    _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d)))
+    d2 = _desc(a, b, c_ref, M, N, K, transB=transB, bias=bias, relu=relu, batch=batch, stream=stream)
+    _lib.check(lib.jst_gemm_ex(ctypes.byref(d2)))
+    torch.cuda.synchronize()
+    got = c_free.cpu().numpy()
+    want = c_ref.cpu().numpy()
+    assert np.isfinite(got).all()
+    # agreement with the allocating entry point, in the suite's metric ...
+    ref64 = want.astype(np.float64)
+    err_vs_ex, where = oracle.max_rel_err(A, B, got if batch > 1 else got[0], ref64 if batch > 1 else ref64[0],
+                                          transB=transB, bias=bias_h)
+    assert err_vs_ex <= TOL, (err_vs_ex, where)
+    # ... and with the fp64 oracle
+    ref = oracle.gemm_f64(A, B, transB=transB, bias=bias_h, relu=relu)
+    err, where = oracle.max_rel_err(A, B, got if batch > 1 else got[0], ref, transB=transB, bias=bias_h)
+    assert err <= TOL, (err, where)
+
+
+def test_noalloc_two_calls_in_a_row_match_allocating_entry_point():
+    # first call: sets the device up and fills the scratch
+    _run_pair(640, 896, 1000, seed=1, transB=True, with_bias=True, relu=True)
+    # second call: other shape and inputs on the scratch the first call left behind
+    _run_pair(333, 517, 250, seed=2, batch=3)
+
+
+def test_noalloc_rejects_requests_beyond_the_fixed_scratch():
+    import torch
+    lib = _lib.load()
+    a = torch.zeros((2048, 2049), device="cuda")
+    b = torch.zeros((2049, 2048), device="cuda")
+    c = torch.zeros((2048, 2048), device="cuda")
+    d = _desc(a, b, c, 2048, 2048, 2049)  # K rounds up to 2052: just over 64 MiB of planes
+    rc = lib.jst_gemm_tc_noalloc(ctypes.byref(d))
+    assert rc == 1
+    assert b"scratch" in lib.jst_last_error()
+    d = _desc(a, b, c, 2048, 2048, 2048)  # exactly 64 MiB: accepted
+    b2 = torch.zeros((2048, 2048), device="cuda")
+    d.B = b2.data_ptr()
+    d.lda = 2049
+    _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d)))
+    torch.cuda.synchronize()
+    assert float(c.abs().max()) == 0.0
