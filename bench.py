@@ -53,7 +53,7 @@ def _peaks() -> dict:
 class ClockSampler:
     """nvidia-smi clock / throttle-reason sampling during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -66,7 +66,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "20",
                  "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, ValueError):
             self.proc = None
@@ -76,7 +76,13 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -88,24 +94,28 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, smax, reasons = [], [], set()
+        sm, smax, power, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        t0, t1 = getattr(self, "t0", 0.0), getattr(self, "t1", float("inf"))
+        for ts, line in self.lines:
+            if not (t0 <= ts <= t1 + 0.05):  # keep samples read during the timed region
+                continue
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
+                sm.append(float(parts[2]))
+                smax.append(float(parts[3]))
+                power.append(float(parts[4]))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[5:9]):
+            for n, v in zip(names, parts[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
 def _traffic_from_profiles() -> tuple[float | None, str | None]:
@@ -184,6 +194,62 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def _e2e(args, A, B, stream) -> dict:
+    """Same GEMM through jst_matmul_host_async: pinned host A, B in, C out."""
+    import torch
+
+    import jstorch_b200
+
+    M, K = A.shape
+    N = B.shape[1]
+    flops = 2.0 * M * N * K
+    a_h = torch.from_numpy(A).pin_memory()
+    b_h = torch.from_numpy(B).pin_memory()
+    c_h = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    for _ in range(max(1, args.warmup)):
+        jstorch_b200.matmul_host_async(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, K, N, stream)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        jstorch_b200.matmul_host_async(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, K, N, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": int(A.nbytes + B.nbytes), "d2h_bytes_per_step": int(M * N * 4),
+           "api": "jst_matmul_host_async (torch.matmul(a, b, M, K, N) entry point), pinned host buffers"}
+
+    return e2e
+
+
+def _ref_gpu_library(args, a, b, c, stream, flops) -> dict:
+    """cuBLAS sgemm with TF32 tensor-op math -- what the reference's
+    native/ops/matmul.cu:12,35 runs -- timed on the same device tensors."""
+    import torch
+
+    try:
+        torch.backends.cuda.matmul.allow_tf32 = True
+        for _ in range(2):
+            torch.matmul(a, b, out=c)
+        torch.cuda.synchronize()
+        r0 = torch.cuda.Event(enable_timing=True)
+        r1 = torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        for _ in range(args.steps):
+            torch.matmul(a, b, out=c)
+        r1.record(stream)
+        torch.cuda.synchronize()
+        ref_ms = r0.elapsed_time(r1) / args.steps
+        return {"impl": "cuBLAS sgemm, TF32 tensor-op math (reference native/ops/matmul.cu:12)",
+                "tflops": flops / (ref_ms * 1e-3) / 1e12, "ms": ref_ms}
+    except Exception as e:  # context only; never fatal
+        return {"error": str(e)}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = False
+
+
 def run_jstorch(args) -> None:
     import torch
 
@@ -200,8 +266,11 @@ def run_jstorch(args) -> None:
     if world > 1:
         raise SystemExit("multi-GPU bench not built yet")
 
-    M = N = K = SIZE
+    M = N = K = args.size
     A, B = synth.config3()
+    if M != SIZE:  # smaller square case (profiling captures): leading block of config 3
+        A = np.ascontiguousarray(A[:M, :K])
+        B = np.ascontiguousarray(B[:K, :N])
     a = torch.from_numpy(A).to(dev)
     b = torch.from_numpy(B).to(dev)
     c = torch.empty((M, N), dtype=torch.float32, device=dev)
@@ -221,11 +290,13 @@ def run_jstorch(args) -> None:
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    clocks.mark_start()
     ev0.record(stream)
     for _ in range(args.steps):
         jstorch_b200.gemm(a, b, out=c, kernel=args.kernel)
     ev1.record(stream)
     torch.cuda.synchronize()
+    clocks.mark_end()
     clk = clocks.stop()
     launches = _lib.launch_count() - n0
     kstats = _lib.profile_read()
@@ -236,23 +307,9 @@ def run_jstorch(args) -> None:
         raise SystemExit("device error word set during the benchmark")
 
     # ---- end to end through the host-array entry point (pinned host buffers)
-    a_h = torch.from_numpy(A).pin_memory()
-    b_h = torch.from_numpy(B).pin_memory()
-    c_h = torch.empty((M, N), dtype=torch.float32).pin_memory()
-    for _ in range(max(1, args.warmup)):
-        jstorch_b200.matmul_host_async(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, K, N, stream)
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        jstorch_b200.matmul_host_async(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, K, N, stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-           "h2d_bytes_per_step": int(A.nbytes + B.nbytes), "d2h_bytes_per_step": int(M * N * 4),
-           "api": "jst_matmul_host_async (torch.matmul(a, b, M, K, N) entry point), pinned host buffers"}
+    e2e = None
+    if not args.no_e2e:
+        e2e = _e2e(args, A, B, stream)
 
     # ---- roofline of the dominant kernel
     peaks = _peaks()
@@ -272,33 +329,15 @@ def run_jstorch(args) -> None:
                 "kernels": {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in kstats.items()}}
 
     # ---- reference GPU library path (cuBLAS sgemm with TF32 math, as the
-    # reference configures it) on the same inputs, for context
-    ref_gpu = None
-    try:
-        torch.backends.cuda.matmul.allow_tf32 = True
-        for _ in range(2):
-            torch.matmul(a, b, out=c)
-        torch.cuda.synchronize()
-        r0 = torch.cuda.Event(enable_timing=True)
-        r1 = torch.cuda.Event(enable_timing=True)
-        r0.record(stream)
-        for _ in range(args.steps):
-            torch.matmul(a, b, out=c)
-        r1.record(stream)
-        torch.cuda.synchronize()
-        torch.backends.cuda.matmul.allow_tf32 = False
-        ref_ms = r0.elapsed_time(r1) / args.steps
-        ref_gpu = {"impl": "cuBLAS sgemm, TF32 tensor-op math (reference native/ops/matmul.cu:12)",
-                   "tflops": flops / (ref_ms * 1e-3) / 1e12, "ms": ref_ms}
-    except Exception as e:  # context only; never fatal
-        ref_gpu = {"error": str(e)}
+    # reference configures it) on the same inputs, for context only
+    ref_gpu = None if args.no_ref_gpu else _ref_gpu_library(args, a, b, c, stream, flops)
 
     line = {
         "metric": "fp32 GEMM TFLOP/s at 8192^3", "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (numpy PCG64, seed 2)",
-        "config": {"workload": "config3: C=A.B, M=N=K=8192, A,B~N(0,1), row-major fp32, device-resident",
+        "config": {"workload": f"config3: C=A.B, M=N=K={M}, A,B~N(0,1), row-major fp32, device-resident",
                    "kernel": args.kernel, "parallelism": "single GPU",
                    "l2": "inputs larger than L2 (A, B, C 256 MiB each; split planes 1 GiB)"},
         "e2e": e2e, "roofline": roofline, "gpu_launches": launches, "clocks": clk,
@@ -313,11 +352,14 @@ def run_jstorch(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["jstorch", "reference"], default="jstorch")
     ap.add_argument("--kernel", choices=["auto", "tc3xtf32", "ffma"], default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-ref-gpu", action="store_true")
+    ap.add_argument("--size", type=int, default=SIZE, help="square GEMM size at N=1 (default 8192)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
