@@ -6,6 +6,7 @@
 
 Outputs (git-ignored, shipped with the source tree):
     jstorch_b200/libjstorch_gemm.so   the C-ABI GEMM library (include/jstorch_gemm.h)
+    jstorch_b200/_core*.so            the host core (Tensor / GradTensor), Python extension
 
 Every CUDA source is compiled for sm_100a only
 (-gencode arch=compute_100a,code=sm_100a); nvcc cross-compiles on a host
@@ -17,6 +18,7 @@ import argparse
 import os
 import subprocess
 import sys
+import sysconfig
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -25,7 +27,8 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 INCLUDE = ROOT / "include"
 
-NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+NVCC = os.environ.get("NVCC", f"{CUDA_HOME}/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
            "--expt-relaxed-constexpr", "-DNDEBUG", f"-I{INCLUDE}"] + ARCH
@@ -72,8 +75,48 @@ def build_gemm(force: bool = False, ptxas_v: bool = False, verbose: bool = False
     return GEMM_LIB
 
 
+CORE = CSRC / "core"
+CORE_CPP = ["tensor.cpp", "autograd.cpp", "allocator.cpp", "binding.cpp"]
+CORE_CU = ["kernels.cu"]
+CORE_HEADERS = ["tensor.h", "autograd.h", "allocator.h", "core_kernels.h"]
+CORE_EXT = PKG / ("_core" + sysconfig.get_config_var("EXT_SUFFIX"))
+CXX = os.environ.get("CXX", "g++")
+
+
+def build_core(force: bool = False, verbose: bool = False) -> Path:
+    """The host core (Tensor / GradTensor) as the Python extension _core,
+    linked against libjstorch_gemm.so (found next to it at run time)."""
+    import pybind11
+
+    BUILD.mkdir(exist_ok=True)
+    headers = [CORE / h for h in CORE_HEADERS] + [INCLUDE / "jstorch_gemm.h"]
+    objs = []
+    incs = [f"-I{INCLUDE}", f"-I{CUDA_HOME}/include", f"-I{sysconfig.get_paths()['include']}",
+            f"-I{pybind11.get_include()}"]
+    for src in CORE_CPP:
+        s = CORE / src
+        o = BUILD / ("core_" + s.stem + ".o")
+        objs.append(o)
+        if force or not _newer(o, [s] + headers + [Path(__file__)]):
+            _run([CXX, "-O2", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-Wall", *incs, "-c", str(s), "-o",
+                  str(o)], verbose)
+    for src in CORE_CU:
+        s = CORE / src
+        o = BUILD / ("core_" + s.stem + ".o")
+        objs.append(o)
+        if force or not _newer(o, [s] + headers + [Path(__file__)]):
+            _run([NVCC, *NVFLAGS, "-c", str(s), "-o", str(o)], verbose)
+    if force or not _newer(CORE_EXT, objs + [GEMM_LIB]):
+        tmp = CORE_EXT.with_suffix(".tmp")
+        _run([NVCC, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), f"-L{PKG}", "-ljstorch_gemm",
+              "-Xlinker", "-rpath,$ORIGIN"], verbose)
+        os.replace(tmp, CORE_EXT)
+    return CORE_EXT
+
+
 def build_all(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> None:
     build_gemm(force=force, ptxas_v=ptxas_v, verbose=verbose)
+    build_core(force=force, verbose=verbose)
 
 
 def main() -> None:
@@ -83,7 +126,7 @@ def main() -> None:
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
     build_all(force=a.force, ptxas_v=a.ptxas_v, verbose=a.verbose)
-    print(f"built {GEMM_LIB.relative_to(ROOT)}")
+    print(f"built {GEMM_LIB.relative_to(ROOT)} {CORE_EXT.relative_to(ROOT)}")
 
 
 if __name__ == "__main__":
