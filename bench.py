@@ -250,6 +250,143 @@ def _ref_gpu_library(args, a, b, c, stream, flops) -> dict:
         torch.backends.cuda.matmul.allow_tf32 = False
 
 
+def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
+    """N > 1: configuration 5's row-sharded GEMM with 8192 rows of A per rank
+    (M = 8192 N, K = N = 8192, A, B ~ U[-1, 1), seed 4).  One step = B
+    broadcast from rank 0 + every rank's GEMM + the all-gather of C, through
+    jst_gemm_rowsharded; device-timed per rank, max over ranks."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from jstorch_b200 import _lib
+    from jstorch_b200 import dist as jdist
+    from jstorch_b200 import synth
+
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))  # host plumbing only
+    dev = torch.device("cuda", local)
+    m_local = K = N = SIZE
+    chunk = args.chunk_rows
+    M = m_local * world
+    plan = jdist.row_plan(world, rank, m_local, chunk)
+    a_host = np.concatenate([synth.config5(rows=blk.rows, row0=blk.global_row0)[0] for blk in plan])
+    b_host = synth.config5(rows=1)[1] if rank == 0 else np.zeros((K, N), np.float32)
+    comm = jdist.Comm.from_process_group(timeout_s=120.0)
+    a = torch.from_numpy(a_host).to(dev)
+    b = torch.from_numpy(b_host).to(dev)
+    c = torch.empty((M, N), dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    flops = 2.0 * M * N * K
+
+    def step():
+        comm.gemm_rowsharded(a, b, c, chunk, root=0, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    comm.sync(stream)
+    dist.barrier()
+    n0 = _lib.launch_count()
+    _lib.profile_enable(True)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    if clocks:
+        clocks.mark_start()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    comm.sync(stream)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.mark_end()
+    dist.barrier()
+    clk = clocks.stop() if clocks else None
+    launches = _lib.launch_count() - n0
+    kstats = _lib.profile_read()
+    _lib.profile_enable(False)
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    t = torch.tensor([ms_local, float(launches)], dtype=torch.float64)
+    tmax = t.clone()
+    dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+    tsum = t.clone()
+    dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+    ms = float(tmax[0])
+    value = flops / (ms * 1e-3) / 1e12
+
+    # end to end: this rank's A rows (and B on the root) in from pinned host
+    # memory, the sharded GEMM, this rank's C rows back to pinned host memory
+    e2e = None
+    if not args.no_e2e:
+        a_h = torch.from_numpy(a_host).pin_memory()
+        b_h = torch.from_numpy(b_host).pin_memory()
+        c_h = torch.empty((m_local, N), dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            a.copy_(a_h, non_blocking=True)
+            if rank == 0:
+                b.copy_(b_h, non_blocking=True)
+            step()
+            for blk in plan:
+                c_h[blk.local_row0:blk.local_row0 + blk.rows].copy_(
+                    c[blk.global_row0:blk.global_row0 + blk.rows], non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        comm.sync(stream)
+        dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        comm.sync(stream)
+        te = torch.tensor([e0.elapsed_time(e1) / args.steps], dtype=torch.float64)
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te[0])
+        e2e = {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": int(a_host.nbytes * world + b_host.nbytes),
+               "d2h_bytes_per_step": int(M * N * 4),
+               "api": "jst_gemm_rowsharded via jstorch_b200.dist.Comm, pinned host A rows / B in, each rank's "
+                      "C rows out (copies on the same stream)"}
+
+    peaks = _peaks()
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    tc = kstats.get("tc_gemm", (0, 0.0))
+    kernel_ms = tc[1] / max(tc[0], 1)
+    per_launch_flops = 2.0 * chunk * N * K
+    achieved = per_launch_flops / (kernel_ms * 1e-3) / 1e12 if kernel_ms > 0 else None
+    roofline = {"kernel": "tc_gemm", "bound": "tensor", "achieved": achieved, "peak": tf32_peak / 3.0,
+                "unit": "TFLOP/s", "frac": (achieved / (tf32_peak / 3.0)) if achieved else None, "traffic": None,
+                "peak_note": f"3xTF32 roofline = (dense bf16 {peaks['bf16_tflops']} TF/s {peaks['source']}, burst)"
+                             f" / 2 / 3; rank 0's launches ({chunk}-row blocks)",
+                "kernel_ms": kernel_ms,
+                "kernels": {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in kstats.items()}}
+    line = {
+        "metric": "fp32 GEMM TFLOP/s at 8192^3", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (numpy PCG64, seed 4)",
+        "config": {"workload": f"config5 row-sharded: C=A.B, M={M} (8192 rows per rank), K=N=8192, "
+                               f"A,B~U[-1,1); B broadcast, C all-gathered (NCCL), {chunk}-row blocks",
+                   "parallelism": f"row-sharded x{world}",
+                   "l2": "inputs larger than L2 (A shard, B 256 MiB each per rank)"},
+        "e2e": e2e, "roofline": roofline, "gpu_launches": int(tsum[1]), "clocks": clk,
+    }
+    comm.destroy()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+
+
 def run_jstorch(args) -> None:
     import torch
 
@@ -264,7 +401,8 @@ def run_jstorch(args) -> None:
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        raise SystemExit("multi-GPU bench not built yet")
+        run_jstorch_sharded(args, rank, world, local)
+        return
 
     M = N = K = args.size
     A, B = synth.config3()
@@ -360,6 +498,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--size", type=int, default=SIZE, help="square GEMM size at N=1 (default 8192)")
+    ap.add_argument("--chunk-rows", type=int, default=2048,
+                    help="row block of the sharded GEMM at N>1 (its all-gather overlaps the next block)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,0 +1,75 @@
+/*
+ * jstorch_dist.h -- C ABI of the multi-GPU (one process per GPU) GEMM path,
+ * library jstorch_b200/libjstorch_dist.so (NCCL over NVLink / NVSwitch).
+ *
+ * No counterpart in the reference, which is single-GPU only.  These entry
+ * points shard the reference's launch_matmul (native/ops/matmul.cu:28) by row
+ * blocks of A and launch_bmm (:40) by batch index across the GPUs of a box.
+ */
+#ifndef JSTORCH_DIST_H
+#define JSTORCH_DIST_H
+
+#include "jstorch_gemm.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct jst_comm jst_comm;
+
+#define JST_COMM_ID_BYTES 128
+
+/* Fill `id` with a new communicator id (call on one rank, share the bytes). */
+int jst_comm_get_unique_id(unsigned char id[JST_COMM_ID_BYTES]);
+
+/*
+ * Create this rank's communicator on the current device.  Non-blocking NCCL
+ * initialisation polled against a host deadline of `timeout_s` seconds: if a
+ * peer never joins, the call aborts the communicator and returns
+ * JST_ERR_TIMEOUT instead of hanging.  The same deadline bounds every later
+ * collective of the communicator.
+ */
+int jst_comm_init(jst_comm** comm, int nranks, int rank, const unsigned char id[JST_COMM_ID_BYTES],
+                  double timeout_s);
+/*
+ * Wait on the host for `stream` to drain, bounded by the communicator's
+ * deadline; on expiry (a collective waiting for a rank that is gone) abort the
+ * communicator and return JST_ERR_TIMEOUT.  Use instead of
+ * cudaStreamSynchronize after sharded calls.
+ */
+int jst_comm_sync(jst_comm* comm, jst_stream_t stream);
+int jst_comm_rank(const jst_comm* comm);
+int jst_comm_size(const jst_comm* comm);
+/* Destroy (or, after an error, abort) the communicator and free its streams. */
+int jst_comm_destroy(jst_comm* comm);
+
+/*
+ * Row-sharded C = A * B over all ranks (every rank receives the full C).
+ *   A_local   [M_local, K] row-major on this rank: row block i (chunk_rows rows,
+ *             i = 0 .. M_local/chunk_rows - 1) holds global rows
+ *             (i * nranks + rank) * chunk_rows + [0, chunk_rows).  With
+ *             chunk_rows == M_local this is plain row-block sharding (rank r
+ *             owns rows [r*M_local, (r+1)*M_local)).
+ *   B         [K, N], valid on `root`; broadcast in place to every rank.
+ *   C_full    [M_local * nranks, N] on every rank.
+ * Each row block is multiplied with the 3 x TF32 tensor-core kernel straight
+ * into its place in C_full; its in-place all-gather runs on a second stream
+ * while the next block is computed.  Asynchronous on `stream`.
+ * M_local must be a multiple of chunk_rows and equal on all ranks.
+ */
+int jst_gemm_rowsharded(jst_comm* comm, const float* A_local, int M_local, int K, float* B, int N, int root,
+                        float* C_full, int chunk_rows, jst_stream_t stream);
+
+/*
+ * Batch-sharded C[b] = A[b] * B[b]: this rank holds batches
+ * [rank * batch_local, (rank + 1) * batch_local) of A and B (packed, as
+ * launch_bmm), computes them into their place in C_full [batch_local * nranks,
+ * M, N] and all-gathers C_full in place.  Asynchronous on `stream`.
+ */
+int jst_bmm_batchsharded(jst_comm* comm, const float* A_local, const float* B_local, int batch_local, int M, int K,
+                         int N, float* C_full, jst_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JSTORCH_DIST_H */

@@ -7,6 +7,7 @@
 Outputs (git-ignored, shipped with the source tree):
     jstorch_b200/libjstorch_gemm.so   the C-ABI GEMM library (include/jstorch_gemm.h)
     jstorch_b200/_core*.so            the host core (Tensor / GradTensor), Python extension
+    jstorch_b200/libjstorch_dist.so   the NCCL sharded GEMMs (include/jstorch_dist.h)
 
 Every CUDA source is compiled for sm_100a only
 (-gencode arch=compute_100a,code=sm_100a); nvcc cross-compiles on a host
@@ -114,9 +115,34 @@ def build_core(force: bool = False, verbose: bool = False) -> Path:
     return CORE_EXT
 
 
+DIST_SOURCES = ["dist.cu"]
+DIST_LIB = PKG / "libjstorch_dist.so"
+
+
+def build_dist(force: bool = False, verbose: bool = False) -> Path:
+    """libjstorch_dist.so: the NCCL sharded GEMMs (include/jstorch_dist.h),
+    linked against libjstorch_gemm.so and the system NCCL."""
+    BUILD.mkdir(exist_ok=True)
+    headers = [CSRC / h for h in GEMM_HEADERS] + [INCLUDE / "jstorch_gemm.h", INCLUDE / "jstorch_dist.h"]
+    objs = []
+    for src in DIST_SOURCES:
+        s = CSRC / src
+        o = BUILD / (s.stem + ".o")
+        objs.append(o)
+        if force or not _newer(o, [s] + headers + [Path(__file__)]):
+            _run([NVCC, *NVFLAGS, "-c", str(s), "-o", str(o)], verbose)
+    if force or not _newer(DIST_LIB, objs + [GEMM_LIB]):
+        tmp = DIST_LIB.with_suffix(".so.tmp")
+        _run([NVCC, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), f"-L{PKG}", "-ljstorch_gemm", "-lnccl",
+              "-Xlinker", "-rpath,$ORIGIN"], verbose)
+        os.replace(tmp, DIST_LIB)
+    return DIST_LIB
+
+
 def build_all(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> None:
     build_gemm(force=force, ptxas_v=ptxas_v, verbose=verbose)
     build_core(force=force, verbose=verbose)
+    build_dist(force=force, verbose=verbose)
 
 
 def main() -> None:
@@ -126,7 +152,7 @@ def main() -> None:
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
     build_all(force=a.force, ptxas_v=a.ptxas_v, verbose=a.verbose)
-    print(f"built {GEMM_LIB.relative_to(ROOT)} {CORE_EXT.relative_to(ROOT)}")
+    print(f"built {GEMM_LIB.relative_to(ROOT)} {CORE_EXT.relative_to(ROOT)} {DIST_LIB.relative_to(ROOT)}")
 
 
 if __name__ == "__main__":

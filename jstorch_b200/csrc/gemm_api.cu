@@ -138,6 +138,15 @@ static int validate(const jst_gemm_desc* d, GemmArgs* a) {
 
 int validate_gemm_desc(const jst_gemm_desc* d, GemmArgs* a) { return validate(d, a); }
 
+int workspace_alloc(size_t bytes, cudaStream_t s, void** out) {
+    int dev = 0;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    return cuda_status(cudaMallocFromPoolAsync(out, bytes ? bytes : 16, g_dev[dev].pool, s), "workspace allocation");
+}
+
+int workspace_free(void* p, cudaStream_t s) { return cuda_status(cudaFreeAsync(p, s), "workspace release"); }
+
 static int gemm(const jst_gemm_desc* d) {
     GemmArgs a;
     int rc = validate(d, &a);

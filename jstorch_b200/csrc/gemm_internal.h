@@ -23,6 +23,10 @@ struct GemmArgs {
 // Check a public descriptor and normalise it into `a` (no device work).
 int validate_gemm_desc(const jst_gemm_desc* d, GemmArgs* a);
 
+// Stream-ordered scratch from the library's per-device pool (checks the device first).
+int workspace_alloc(size_t bytes, cudaStream_t s, void** out);
+int workspace_free(void* p, cudaStream_t s);
+
 // Record `status` with `msg` as the calling thread's last status; returns status.
 int set_status(int status, const char* msg);
 
@@ -32,6 +36,14 @@ uint32_t* device_error_word();
 // 3 x TF32 tcgen05 path
 size_t tc_workspace_bytes(const GemmArgs& a);
 int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s);
+// Split pass alone: `rows` x K operand rows (K-major source when kmajor, else
+// stored [K, rows]) into hi / lo planes [batch][rows][Kp], Kp = K rounded up to 4.
+int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows, int K, int batch, float* hi,
+             float* lo, cudaStream_t s);
+// Tensor-core kernel alone on existing planes (A planes M rows, B planes N rows).
+int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
+                   int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
+                   cudaStream_t s);
 
 // FFMA SIMT path (no workspace)
 int ffma_gemm_run(const GemmArgs& a, cudaStream_t s);

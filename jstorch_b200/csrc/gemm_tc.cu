@@ -347,31 +347,20 @@ size_t tc_workspace_bytes(const GemmArgs& a) {
     return 2 * Kp * ((size_t)a.M + (size_t)a.N) * (size_t)a.batch * sizeof(float);
 }
 
-// Split both operands into `workspace` and run the tensor-core kernel;
-// `err` receives the kernel's timeout flag.
-static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cudaStream_t s) {
+int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows, int K, int batch, float* hi,
+             float* lo, cudaStream_t s) {
+    const int rc = tc::launch_split(src, kmajor != 0, ld, sstride, rows, K, (K + 3) & ~3, batch, hi, lo, s);
+    return rc ? set_status(rc, "split pass failed to launch") : JST_OK;
+}
+
+int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
+                   int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
+                   cudaStream_t s) {
     using namespace tc;
-    const int Kp = (a.K + 3) & ~3;
-    float* ws = static_cast<float*>(workspace);
-    const size_t a_plane = (size_t)a.batch * a.M * Kp;
-    const size_t b_plane = (size_t)a.batch * a.N * Kp;
-    float* a_hi = ws;
-    float* a_lo = a_hi + a_plane;
-    float* b_hi = a_lo + a_plane;
-    float* b_lo = b_hi + b_plane;
-
-    // op(A) rows are M: K-major unless A is stored transposed.
-    int rc = launch_split(a.A, !a.transA, a.lda, a.strideA, a.M, a.K, Kp, a.batch, a_hi, a_lo, s);
-    if (rc) return set_status(rc, "split of A failed to launch");
-    // op(B)^T rows are N: K-major when B is stored [N, K] (transB).
-    rc = launch_split(a.B, a.transB, a.ldb, a.strideB, a.N, a.K, Kp, a.batch, b_hi, b_lo, s);
-    if (rc) return set_status(rc, "split of B failed to launch");
-
+    const int Kp = (K + 3) & ~3;
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-    if (!make_plane_map(&m_ahi, a_hi, a.K, a.M, a.batch, Kp, BM) ||
-        !make_plane_map(&m_alo, a_lo, a.K, a.M, a.batch, Kp, BM) ||
-        !make_plane_map(&m_bhi, b_hi, a.K, a.N, a.batch, Kp, BN) ||
-        !make_plane_map(&m_blo, b_lo, a.K, a.N, a.batch, Kp, BN))
+    if (!make_plane_map(&m_ahi, a_hi, K, M, batch, Kp, BM) || !make_plane_map(&m_alo, a_lo, K, M, batch, Kp, BM) ||
+        !make_plane_map(&m_bhi, b_hi, K, N, batch, Kp, BN) || !make_plane_map(&m_blo, b_lo, K, N, batch, Kp, BN))
         return set_status(JST_ERR_CUDA, "cuTensorMapEncodeTiled failed");
 
     static bool attr_set[64] = {};
@@ -384,13 +373,13 @@ static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cud
         attr_set[dev] = true;
     }
     Params p;
-    p.M = a.M; p.N = a.N; p.K = a.K; p.batch = a.batch;
-    p.C = a.C; p.ldc = a.ldc; p.strideC = a.strideC;
-    p.bias = a.bias; p.relu = a.relu;
-    p.tiles_m = (a.M + BM - 1) / BM;
-    p.tiles_n = (a.N + BN - 1) / BN;
+    p.M = M; p.N = N; p.K = K; p.batch = batch;
+    p.C = C; p.ldc = ldc; p.strideC = strideC;
+    p.bias = bias; p.relu = relu;
+    p.tiles_m = (M + BM - 1) / BM;
+    p.tiles_n = (N + BN - 1) / BN;
     p.err = err;
-    const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * a.batch;
+    const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * batch;
     if (grid > 0x7fffffff) return set_status(JST_ERR_ARG, "tc: too many tiles");
     {
         ProfScope prof(s, KID_TC_GEMM);
@@ -398,6 +387,27 @@ static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cud
     }
     if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "tc_gemm_kernel launch failed");
     return JST_OK;
+}
+
+// Split both operands into `workspace` and run the tensor-core kernel;
+// `err` receives the kernel's timeout flag.
+static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cudaStream_t s) {
+    const int Kp = (a.K + 3) & ~3;
+    float* ws = static_cast<float*>(workspace);
+    const size_t a_plane = (size_t)a.batch * a.M * Kp;
+    const size_t b_plane = (size_t)a.batch * a.N * Kp;
+    float* a_hi = ws;
+    float* a_lo = a_hi + a_plane;
+    float* b_hi = a_lo + a_plane;
+    float* b_lo = b_hi + b_plane;
+    // op(A) rows are M: K-major unless A is stored transposed.
+    int rc = tc_split(a.A, !a.transA, a.lda, a.strideA, a.M, a.K, a.batch, a_hi, a_lo, s);
+    if (rc) return rc;
+    // op(B)^T rows are N: K-major when B is stored [N, K] (transB).
+    rc = tc_split(a.B, a.transB, a.ldb, a.strideB, a.N, a.K, a.batch, b_hi, b_lo, s);
+    if (rc) return rc;
+    return tc_gemm_planes(a_hi, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, a.C, a.ldc, a.strideC, a.bias, a.relu, err,
+                          s);
 }
 
 int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {

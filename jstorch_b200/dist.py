@@ -1,0 +1,129 @@
+"""Multi-GPU face of the path: one process per GPU, libjstorch_dist.so
+(include/jstorch_dist.h) for the NCCL row-sharded GEMM and batch-sharded bmm.
+
+torch.distributed (any backend; gloo is enough) is used only to hand the
+communicator id from rank 0 to the others; all data moves through the
+library's own NCCL communicator.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from pathlib import Path
+
+from . import _lib
+
+LIB_PATH = Path(__file__).resolve().parent / "libjstorch_dist.so"
+ID_BYTES = 128
+_dlib = None
+
+
+def load() -> ctypes.CDLL:
+    global _dlib
+    if _dlib is None:
+        _lib.load()  # libjstorch_gemm.so first (status messages live there)
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is not built; run `python -m jstorch_b200.build`")
+        d = ctypes.CDLL(str(LIB_PATH))
+        vp, ci, cd = ctypes.c_void_p, ctypes.c_int, ctypes.c_double
+        d.jst_comm_get_unique_id.restype = ci
+        d.jst_comm_get_unique_id.argtypes = [ctypes.c_char_p]
+        d.jst_comm_init.restype = ci
+        d.jst_comm_init.argtypes = [ctypes.POINTER(vp), ci, ci, ctypes.c_char_p, cd]
+        d.jst_comm_sync.restype = ci
+        d.jst_comm_sync.argtypes = [vp, vp]
+        d.jst_comm_destroy.restype = ci
+        d.jst_comm_destroy.argtypes = [vp]
+        d.jst_comm_rank.restype = ci
+        d.jst_comm_rank.argtypes = [vp]
+        d.jst_comm_size.restype = ci
+        d.jst_comm_size.argtypes = [vp]
+        d.jst_gemm_rowsharded.restype = ci
+        d.jst_gemm_rowsharded.argtypes = [vp, vp, ci, ci, vp, ci, ci, vp, ci, vp]
+        d.jst_bmm_batchsharded.restype = ci
+        d.jst_bmm_batchsharded.argtypes = [vp, vp, vp, ci, ci, ci, ci, vp, vp]
+        _dlib = d
+    return _dlib
+
+
+@dataclass(frozen=True)
+class RowBlock:
+    local_row0: int   # first row of the block in this rank's A_local / C rows
+    global_row0: int  # first row of the block in the global A / C_full
+    rows: int
+
+
+def row_plan(nranks: int, rank: int, m_local: int, chunk_rows: int) -> list[RowBlock]:
+    """Row blocks owned by `rank` in jst_gemm_rowsharded's block-cyclic layout:
+    block i of rank r holds global rows (i * nranks + r) * chunk_rows + [0, chunk_rows)."""
+    if chunk_rows < 1 or m_local % chunk_rows:
+        raise ValueError("m_local must be a positive multiple of chunk_rows")
+    return [RowBlock(i * chunk_rows, (i * nranks + rank) * chunk_rows, chunk_rows)
+            for i in range(m_local // chunk_rows)]
+
+
+class Comm:
+    """A rank's NCCL communicator (jst_comm) on the current CUDA device."""
+
+    def __init__(self, nranks: int, rank: int, unique_id: bytes, timeout_s: float = 60.0):
+        if len(unique_id) != ID_BYTES:
+            raise ValueError("communicator id must be 128 bytes")
+        handle = ctypes.c_void_p()
+        _lib.check(load().jst_comm_init(ctypes.byref(handle), nranks, rank, unique_id, float(timeout_s)))
+        self.handle = handle
+        self.nranks, self.rank = nranks, rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(ID_BYTES)
+        _lib.check(load().jst_comm_get_unique_id(buf))
+        return buf.raw
+
+    @classmethod
+    def from_process_group(cls, timeout_s: float = 60.0) -> "Comm":
+        """Create the communicator of every rank of torch.distributed's default group."""
+        import torch.distributed as dist
+
+        rank, world = dist.get_rank(), dist.get_world_size()
+        obj = [cls.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        return cls(world, rank, obj[0], timeout_s)
+
+    def sync(self, stream) -> None:
+        """Host wait for `stream`, bounded by the communicator deadline."""
+        _lib.check(load().jst_comm_sync(self.handle, stream.cuda_stream))
+
+    def destroy(self) -> None:
+        if self.handle:
+            rc = load().jst_comm_destroy(self.handle)
+            self.handle = None
+            _lib.check(rc)
+
+    def gemm_rowsharded(self, a_local, b, c_full, chunk_rows: int, root: int = 0, stream=None) -> None:
+        """C_full = A . B with A block-cyclically row-sharded (see row_plan); b is
+        broadcast in place from `root`.  Device tensors: a_local [M_local, K],
+        b [K, N], c_full [M_local * nranks, N], all contiguous fp32."""
+        import torch
+
+        for t in (a_local, b, c_full):
+            if not (t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()):
+                raise ValueError("operands must be contiguous float32 CUDA tensors")
+        m_local, k = a_local.shape
+        n = b.shape[1]
+        if b.shape[0] != k or tuple(c_full.shape) != (m_local * self.nranks, n):
+            raise ValueError("shape mismatch")
+        st = stream if stream is not None else torch.cuda.current_stream()
+        _lib.check(load().jst_gemm_rowsharded(self.handle, a_local.data_ptr(), m_local, k, b.data_ptr(), n, root,
+                                              c_full.data_ptr(), chunk_rows, st.cuda_stream))
+
+    def bmm_batchsharded(self, a_local, b_local, c_full, stream=None) -> None:
+        """c_full[rank*bl:(rank+1)*bl] = a_local . b_local, then all-gathered in place."""
+        import torch
+
+        bl, m, k = a_local.shape
+        n = b_local.shape[2]
+        if b_local.shape[:2] != (bl, k) or tuple(c_full.shape) != (bl * self.nranks, m, n):
+            raise ValueError("shape mismatch")
+        st = stream if stream is not None else torch.cuda.current_stream()
+        _lib.check(load().jst_bmm_batchsharded(self.handle, a_local.data_ptr(), b_local.data_ptr(), bl, m, k, n,
+                                               c_full.data_ptr(), st.cuda_stream))
