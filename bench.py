@@ -387,6 +387,136 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     dist.destroy_process_group()
 
 
+def _time_device(fn, steps: int, warmup: int, stream) -> float:
+    """ms per call of fn(), CUDA events on `stream`, after `warmup` calls."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_config(args) -> None:
+    """Secondary measurements (one JSON line each) for the other BASELINE
+    configurations; the headline line is configuration 3 (default)."""
+    import torch
+
+    import jstorch_b200
+    from jstorch_b200 import _lib, synth
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    peaks = _peaks()
+    out = {"config_id": args.config, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "dtype": "f32",
+           "data": "synthetic (numpy PCG64)"}
+    if args.config == 1:
+        A, B = synth.config1()
+        flops = 2.0 * 512 ** 3
+        a, b = torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev)
+        c = torch.empty((512, 512), device=dev)
+        res = {}
+        for k in ("auto", "tc3xtf32", "ffma"):
+            ms = _time_device(lambda: jstorch_b200.gemm(a, b, out=c, kernel=k), args.steps, args.warmup, stream)
+            res[k] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12}
+        ah, bh = A.reshape(-1), B.reshape(-1)
+        for _ in range(args.warmup):
+            jstorch_b200.torch.matmul(ah, bh, 512, 512, 512)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            jstorch_b200.torch.matmul(ah, bh, 512, 512, 512)
+        host_ms = (time.perf_counter() - t0) / args.steps * 1e3
+        out.update({"metric": "config1 512^3 GEMM", "unit": "TFLOP/s", "value": res["auto"]["tflops"],
+                    "device": res, "selected": jstorch_b200.select_kernel(512, 512, 512),
+                    "e2e": {"api": "torch.matmul(a, b, 512, 512, 512) (jst_matmul_host, pageable numpy arrays, "
+                                   "synchronous; wall clock per call)",
+                            "ms": host_ms, "value": flops / (host_ms * 1e-3) / 1e12, "unit": "TFLOP/s"}})
+    elif args.config == 2:
+        from jstorch_b200 import _core, nn
+
+        x, ws, bs = synth.config2()
+        model = nn.Sequential(nn.Linear(784, 1024), nn.ReLU(), nn.Linear(1024, 1024), nn.ReLU(),
+                              nn.Linear(1024, 10))
+        st = {}
+        for i, (w, bb) in zip((0, 2, 4), zip(ws, bs)):
+            st[f"{i}.weight"] = _core.Tensor.fromBuffer(w)
+            st[f"{i}.bias"] = _core.Tensor.fromBuffer(bb)
+        model.load_state_dict(st)
+        model._init_grad()
+        xt = _core.GradTensor(_core.Tensor.fromBuffer(x), False)
+
+        def step():
+            y = model(xt)
+            y.backward()
+
+        legacy = torch.cuda.default_stream(dev)  # the host core enqueues on the legacy default stream
+        ms = _time_device(step, args.steps, args.warmup, legacy)
+        flops = 2.448e9
+        out.update({"metric": "config2 MLP forward+backward (batch 256, 784-1024-1024-10)", "unit": "ms",
+                    "value": ms, "higher_is_better": False, "tflops": flops / (ms * 1e-3) / 1e12,
+                    "note": "host core Tensor/GradTensor path, eager (per-op launches); 2.448 GFLOP algorithmic"})
+    elif args.config == 3:
+        A, B = synth.config3()
+        M = N = K = 8192
+        flops = 2.0 * M * N * K
+        a, b = torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev)
+        c = torch.empty((M, N), device=dev)
+        _lib.profile_enable(True)
+        ms = _time_device(lambda: jstorch_b200.gemm(a, b, out=c, kernel=args.kernel), args.steps, args.warmup,
+                          stream)
+        ks = _lib.profile_read()
+        _lib.profile_enable(False)
+        res = {"metric": f"config3 8192^3 GEMM, kernel {args.kernel}", "unit": "TFLOP/s",
+               "value": flops / (ms * 1e-3) / 1e12, "ms": ms,
+               "kernels": {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in ks.items()}}
+        if args.kernel == "ffma":
+            simt_peak = 148 * 128 * 2 * 1965e6 / 1e12
+            fk = ks.get("ffma_gemm", (1, ms))
+            ach = flops / (fk[1] / max(fk[0], 1) * 1e-3) / 1e12
+            res["roofline"] = {"kernel": "ffma_gemm", "bound": "fma", "achieved": ach, "peak": simt_peak,
+                               "frac": ach / simt_peak, "unit": "TFLOP/s",
+                               "peak_note": "FP32 SIMT peak 148 SMs x 128 lanes x 2 flop x 1965 MHz (nominal)"}
+        out.update(res)
+    elif args.config == 4:
+        q, kt, p, v = synth.config4()
+        tq, tk, tp, tv = (torch.from_numpy(t).to(dev) for t in (q, kt, p, v))
+        s_ = torch.empty((64, 512, 512), device=dev)
+        o_ = torch.empty((64, 512, 64), device=dev)
+        res = {}
+        for name, x, y, z, nbytes in (("scores [512x64].[64x512]", tq, tk, s_, (q.nbytes + kt.nbytes + s_.numel() * 4)),
+                                      ("output [512x512].[512x64]", tp, tv, o_, (p.nbytes + v.nbytes + o_.numel() * 4))):
+            flops = 2.0 * 64 * 512 * 512 * 64
+            for k in ("auto", "tc3xtf32", "ffma"):
+                ms = _time_device(lambda: jstorch_b200.gemm(x, y, out=z, kernel=k), args.steps, args.warmup, stream)
+                res[f"{name} {k}"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+                                      "gbs": nbytes / (ms * 1e-3) / 1e9,
+                                      "hbm_frac": nbytes / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"]}
+        out.update({"metric": "config4 strided-batched attention shapes (batch 64)", "unit": "TFLOP/s",
+                    "value": res["scores [512x64].[64x512] auto"]["tflops"], "results": res,
+                    "note": f"compulsory bytes vs measured HBM {peaks['hbm_gbs']} GB/s"})
+    elif args.config == 5:
+        A, B = synth.config5()
+        M, K, N = A.shape[0], A.shape[1], B.shape[1]
+        flops = 2.0 * M * N * K
+        a, b = torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev)
+        del A
+        c = torch.empty((M, N), device=dev)
+        ms = _time_device(lambda: jstorch_b200.gemm(a, b, out=c, kernel=args.kernel), args.steps, args.warmup,
+                          stream)
+        out.update({"metric": "config5 65536x8192x8192 GEMM on one GPU (strong-scaling reference point)",
+                    "unit": "TFLOP/s", "value": flops / (ms * 1e-3) / 1e12, "ms": ms})
+    print(json.dumps(out), flush=True)
+
+
 def run_jstorch(args) -> None:
     import torch
 
@@ -498,6 +628,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--size", type=int, default=SIZE, help="square GEMM size at N=1 (default 8192)")
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
+                    help="secondary measurement of one BASELINE configuration (0: the headline line)")
     ap.add_argument("--chunk-rows", type=int, default=2048,
                     help="row block of the sharded GEMM at N>1 (its all-gather overlaps the next block)")
     args = ap.parse_args()
@@ -505,6 +637,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.config:
+        run_config(args)
     else:
         run_jstorch(args)
 

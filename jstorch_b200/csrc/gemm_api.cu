@@ -94,10 +94,13 @@ uint32_t* device_error_word() {
 
 // ---------------------------------------------------------------- dispatch
 static bool use_tc(const GemmArgs& a) {
-    // The split pass costs one read of each operand plus two plane writes; the
-    // tensor-core kernel needs whole 128 x 256 tiles to pay for it.
+    // The split pass costs one read of each operand plus two plane writes, and
+    // the tensor-core kernel needs many 128 x 256 tiles to fill 148 SMs.
+    // Measured on B200 (fp32 in / out): FFMA is as fast or faster up to about
+    // 2^28 multiply-adds (512^3, the nn.Linear layers of the MLP config); the
+    // tensor-core kernel wins from 2^30 (64 x 512x512x64 batched, 2048^3 and up).
     const double macs = (double)a.M * a.N * a.K * a.batch;
-    return a.M >= 64 && a.N >= 64 && a.K >= 32 && macs >= 32.0e6;
+    return a.M >= 64 && a.N >= 64 && a.K >= 32 && macs >= 1073741824.0;
 }
 
 static int validate(const jst_gemm_desc* d, GemmArgs* a) {
@@ -181,11 +184,90 @@ static int gemm(const jst_gemm_desc* d) {
 struct HostStage {
     std::mutex mu;
     int dev = -1;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;  // compute stream of synchronous calls
+    cudaStream_t h2d = nullptr;     // copy streams of the pipelined path
+    cudaStream_t d2h = nullptr;
+    std::vector<cudaEvent_t> ev;
     float* d_buf = nullptr;  // A | B | C
     size_t d_cap = 0;        // floats
 };
 static HostStage g_host[64];
+
+// Pipelined host GEMM for large tensor-core shapes: A is moved and multiplied
+// in row chunks so that its host->device copies (copy stream h2d), the split +
+// GEMM of the previous chunk (compute stream st) and the device->host copy of
+// C chunks (copy stream d2h) overlap.  B is copied and split once first.
+// All three streams are ordered after the caller's earlier work on st, and st
+// is ordered after the last C chunk has reached the host buffer.
+static int host_matmul_pipelined(HostStage& h, const float* a, const float* b, float* c, int M, int K, int N,
+                                 float* dA, float* dB, float* dC, cudaStream_t st) {
+    int rc;
+    if (!h.h2d) {
+        rc = cuda_status(cudaStreamCreateWithFlags(&h.h2d, cudaStreamNonBlocking), "stream create");
+        if (rc) return rc;
+        rc = cuda_status(cudaStreamCreateWithFlags(&h.d2h, cudaStreamNonBlocking), "stream create");
+        if (rc) return rc;
+    }
+    const int64_t Kp = (K + 3) & ~3;
+    int64_t R = ((int64_t)M + 7) / 8;
+    R = std::max<int64_t>(1024, (R + 127) / 128 * 128);
+    const int nchunks = (int)((M + R - 1) / R);
+    const size_t nev = 3 + 2 * (size_t)nchunks;
+    while (h.ev.size() < nev) {
+        cudaEvent_t e;
+        rc = cuda_status(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event create");
+        if (rc) return rc;
+        h.ev.push_back(e);
+    }
+    cudaEvent_t ev_entry = h.ev[0], ev_b = h.ev[1], ev_done = h.ev[2];
+    auto ev_a = [&](int i) { return h.ev[3 + 2 * i]; };
+    auto ev_c = [&](int i) { return h.ev[4 + 2 * i]; };
+    const size_t a_plane = (size_t)M * Kp, b_plane = (size_t)N * Kp;
+    void* ws = nullptr;
+    rc = workspace_alloc((2 * a_plane + 2 * b_plane) * sizeof(float), st, &ws);
+    if (rc) return rc;
+    float* a_hi = static_cast<float*>(ws);
+    float* a_lo = a_hi + a_plane;
+    float* b_hi = a_lo + a_plane;
+    float* b_lo = b_hi + b_plane;
+    uint32_t* err = device_error_word();
+
+    rc = cuda_status(cudaEventRecord(ev_entry, st), "event record");
+    if (!rc) rc = cuda_status(cudaStreamWaitEvent(h.h2d, ev_entry, 0), "stream wait");
+    if (!rc) rc = cuda_status(cudaStreamWaitEvent(h.d2h, ev_entry, 0), "stream wait");
+    if (!rc) rc = cuda_status(cudaMemcpyAsync(dB, b, (size_t)K * N * sizeof(float), cudaMemcpyHostToDevice, h.h2d),
+                              "H2D B");
+    if (!rc) rc = cuda_status(cudaEventRecord(ev_b, h.h2d), "event record");
+    if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, ev_b, 0), "stream wait");
+    if (!rc) rc = tc_split(dB, 0, N, 0, N, K, 1, b_hi, b_lo, st);
+    // inputs and compute first: with pageable host memory each H2D copy blocks
+    // the host, and the C copies must not be queued ahead of them
+    for (int i = 0; i < nchunks && !rc; ++i) {
+        const int64_t r0 = (int64_t)i * R;
+        const int rows = (int)std::min<int64_t>(R, M - r0);
+        rc = cuda_status(cudaMemcpyAsync(dA + r0 * K, a + r0 * K, (size_t)rows * K * sizeof(float),
+                                         cudaMemcpyHostToDevice, h.h2d), "H2D A chunk");
+        if (!rc) rc = cuda_status(cudaEventRecord(ev_a(i), h.h2d), "event record");
+        if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, ev_a(i), 0), "stream wait");
+        if (!rc) rc = tc_split(dA + r0 * K, 1, K, 0, rows, K, 1, a_hi + r0 * Kp, a_lo + r0 * Kp, st);
+        if (!rc)
+            rc = tc_gemm_planes(a_hi + r0 * Kp, a_lo + r0 * Kp, b_hi, b_lo, rows, N, K, 1, dC + r0 * N, N, 0, nullptr,
+                                0, err, st);
+        if (!rc) rc = cuda_status(cudaEventRecord(ev_c(i), st), "event record");
+    }
+    for (int i = 0; i < nchunks && !rc; ++i) {
+        const int64_t r0 = (int64_t)i * R;
+        const int rows = (int)std::min<int64_t>(R, M - r0);
+        rc = cuda_status(cudaStreamWaitEvent(h.d2h, ev_c(i), 0), "stream wait");
+        if (!rc)
+            rc = cuda_status(cudaMemcpyAsync(c + r0 * N, dC + r0 * N, (size_t)rows * N * sizeof(float),
+                                             cudaMemcpyDeviceToHost, h.d2h), "D2H C chunk");
+    }
+    if (!rc) rc = cuda_status(cudaEventRecord(ev_done, h.d2h), "event record");
+    if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, ev_done, 0), "stream wait");
+    const int frc = workspace_free(ws, st);
+    return rc ? rc : frc;
+}
 
 // Host-array GEMM: stage a and b to device buffers cached per device, run the
 // GEMM, copy C back.  sync: on the library's own stream, waiting for the
@@ -224,6 +306,17 @@ static int host_matmul(const float* a, const float* b, float* c, int M, int K, i
     float* dA = h.d_buf;
     float* dB = dA + up4(na);
     float* dC = dB + up4(nb);
+    {
+        jst_gemm_desc probe;
+        jst_gemm_desc_init(&probe, M, N, K, dA, dB, dC);
+        GemmArgs pa{};
+        validate(&probe, &pa);
+        if (M >= 2048 && K > 0 && N > 0 && use_tc(pa)) {
+            rc = host_matmul_pipelined(h, a, b, c, M, K, N, dA, dB, dC, st);
+            if (rc) return rc;
+            goto done;
+        }
+    }
     if (na) {
         rc = cuda_status(cudaMemcpyAsync(dA, a, na * sizeof(float), cudaMemcpyHostToDevice, st), "H2D A");
         if (rc) return rc;
@@ -241,6 +334,7 @@ static int host_matmul(const float* a, const float* b, float* c, int M, int K, i
         rc = cuda_status(cudaMemcpyAsync(c, dC, nc * sizeof(float), cudaMemcpyDeviceToHost, st), "D2H C");
         if (rc) return rc;
     }
+done:
     if (!sync) return set_status(JST_OK, nullptr);
     rc = cuda_status(cudaStreamSynchronize(st), "matmul synchronise");
     if (rc) return rc;

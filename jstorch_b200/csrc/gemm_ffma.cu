@@ -33,8 +33,10 @@ struct Params {
     int vecA, vecB, vecC;
 };
 
+// Two CTAs per SM: the register cap (128 for 256 threads) keeps 16 warps
+// resident to hide the shared-memory and global-load latency.
 template <int BM, int BN, int BK, int RM, int RN, bool TA, bool TB>
-__global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)))
+__global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
     ffma_gemm_kernel(const Params p) {
     constexpr int TX = BN / (4 * RN);
     constexpr int TY = BM / (4 * RM);

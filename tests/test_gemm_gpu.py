@@ -191,5 +191,35 @@ def test_config4_batched_attention_shapes(jst):
 
 def test_kernel_choice_heuristic(jst):
     assert jst.select_kernel(8192, 8192, 8192) == "tc3xtf32"
+    assert jst.select_kernel(2048, 2048, 2048) == "tc3xtf32"
+    assert jst.select_kernel(512, 64, 512, batch=64) == "tc3xtf32"
+    assert jst.select_kernel(512, 512, 512) == "ffma"
+    assert jst.select_kernel(256, 1024, 784) == "ffma"
     assert jst.select_kernel(256, 10, 1024) == "ffma"
     assert jst.select_kernel(2, 4, 3) == "ffma"
+
+
+@pytest.mark.parametrize("pinned", [False, True])
+def test_host_matmul_pipelined_chunks(jst, pinned):
+    """Large host-array products take the chunked path (H2D / GEMM / D2H
+    overlapped on three streams); a ragged last chunk and both pageable and
+    pinned host buffers must give the same product."""
+    import torch
+    rng = np.random.default_rng(21)
+    M, K, N = 2304, 520, 648  # chunks of 1024, 1024, 256 rows
+    A = rng.standard_normal((M, K), dtype=np.float32)
+    B = rng.standard_normal((K, N), dtype=np.float32)
+    if pinned:
+        a_h = torch.from_numpy(A).pin_memory()
+        b_h = torch.from_numpy(B).pin_memory()
+        c_h = torch.full((M, N), float("nan")).pin_memory()
+        from jstorch_b200.gemm import matmul_host_ptr
+        matmul_host_ptr(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, K, N)
+        C = c_h.numpy()
+    else:
+        C = jst.torch.matmul(A, B, M, K, N).reshape(M, N)
+    rows = np.array([0, 1, 1023, 1024, 2047, 2048, 2303], np.int32)
+    ref = oracle.gemm_f64(A, B, rows=rows)
+    err, where = oracle.max_rel_err(A, B, C, ref, rows=rows)
+    assert err <= TOL, (err, where)
+    assert np.isfinite(C).all()
