@@ -275,7 +275,16 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     comm = jdist.Comm.from_process_group(timeout_s=120.0)
     a = torch.from_numpy(a_host).to(dev)
     b = torch.from_numpy(b_host).to(dev)
-    c = torch.empty((M, N), dtype=torch.float32, device=dev)
+    # C in a multicast-backed buffer: the all-gather of C is fused into the
+    # GEMM epilogue (multimem stores through the NVLink switch)
+    symm, gather = None, "NCCL all-gather rounds overlapped with the next block"
+    if not args.nccl_allgather:
+        try:
+            symm = comm.symm_alloc(M * N * 4)
+            gather = "fused into the GEMM epilogue (multimem stores to a multicast-backed C)"
+        except _lib.JstError as e:
+            gather = f"NCCL all-gather rounds (multicast buffer unavailable: {e})"
+    c = symm.tensor((M, N)) if symm else torch.empty((M, N), dtype=torch.float32, device=dev)
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     flops = 2.0 * M * N * K
@@ -376,11 +385,15 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (numpy PCG64, seed 4)",
         "config": {"workload": f"config5 row-sharded: C=A.B, M={M} (8192 rows per rank), K=N=8192, "
-                               f"A,B~U[-1,1); B broadcast, C all-gathered (NCCL), {chunk}-row blocks",
+                               f"A,B~U[-1,1); B broadcast (NCCL), C gathered on every rank, {chunk}-row blocks",
+                   "c_gather": gather,
                    "parallelism": f"row-sharded x{world}",
                    "l2": "inputs larger than L2 (A shard, B 256 MiB each per rank)"},
         "e2e": e2e, "roofline": roofline, "gpu_launches": int(tsum[1]), "clocks": clk,
     }
+    del c
+    if symm:
+        symm.free()
     comm.destroy()
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -630,7 +643,9 @@ def main() -> None:
     ap.add_argument("--size", type=int, default=SIZE, help="square GEMM size at N=1 (default 8192)")
     ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
                     help="secondary measurement of one BASELINE configuration (0: the headline line)")
-    ap.add_argument("--chunk-rows", type=int, default=2048,
+    ap.add_argument("--nccl-allgather", action="store_true",
+                    help="N>1: gather C with NCCL all-gathers instead of the fused multicast epilogue")
+    ap.add_argument("--chunk-rows", type=int, default=1024,
                     help="row block of the sharded GEMM at N>1 (its all-gather overlaps the next block)")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -44,6 +44,20 @@ int jst_comm_size(const jst_comm* comm);
 int jst_comm_destroy(jst_comm* comm);
 
 /*
+ * Multicast-backed buffer: `bytes` of device memory on every rank of the
+ * communicator, bound to one NVLink-switch multicast object, so that a single
+ * store through the multicast address lands in every rank's copy.  Collective:
+ * every rank calls it in the same order with the same size.  Needs a device
+ * with multicast support (CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED) and all
+ * ranks on one node; otherwise returns JST_ERR_UNSUPPORTED.  *local receives
+ * this rank's ordinary device pointer to its copy.
+ */
+typedef struct jst_symm jst_symm;
+int jst_symm_alloc(jst_comm* comm, size_t bytes, jst_symm** out, void** local);
+/* Collective release (all ranks, after their last use). */
+int jst_symm_free(jst_symm* buf);
+
+/*
  * Row-sharded C = A * B over all ranks (every rank receives the full C).
  *   A_local   [M_local, K] row-major on this rank: row block i (chunk_rows rows,
  *             i = 0 .. M_local/chunk_rows - 1) holds global rows
@@ -54,7 +68,10 @@ int jst_comm_destroy(jst_comm* comm);
  *   C_full    [M_local * nranks, N] on every rank.
  * Each row block is multiplied with the 3 x TF32 tensor-core kernel straight
  * into its place in C_full; its in-place all-gather runs on a second stream
- * while the next block is computed.  Asynchronous on `stream`.
+ * while the next block is computed.  When C_full lies in a jst_symm buffer the
+ * all-gather is fused into the GEMM instead: the kernel's epilogue stores each
+ * tile once through the multicast address and the switch delivers it to every
+ * rank (no collective for C, one barrier at the end).  Asynchronous on `stream`.
  * M_local must be a multiple of chunk_rows and equal on all ranks.
  */
 int jst_gemm_rowsharded(jst_comm* comm, const float* A_local, int M_local, int K, float* B, int N, int root,

@@ -115,7 +115,7 @@ def build_core(force: bool = False, verbose: bool = False) -> Path:
     return CORE_EXT
 
 
-DIST_SOURCES = ["dist.cu"]
+DIST_SOURCES = ["dist.cu", "symm.cu"]
 DIST_LIB = PKG / "libjstorch_dist.so"
 
 
@@ -123,7 +123,8 @@ def build_dist(force: bool = False, verbose: bool = False) -> Path:
     """libjstorch_dist.so: the NCCL sharded GEMMs (include/jstorch_dist.h),
     linked against libjstorch_gemm.so and the system NCCL."""
     BUILD.mkdir(exist_ok=True)
-    headers = [CSRC / h for h in GEMM_HEADERS] + [INCLUDE / "jstorch_gemm.h", INCLUDE / "jstorch_dist.h"]
+    headers = [CSRC / h for h in GEMM_HEADERS + ["dist_internal.h"]] + [INCLUDE / "jstorch_gemm.h",
+                                                                         INCLUDE / "jstorch_dist.h"]
     objs = []
     for src in DIST_SOURCES:
         s = CSRC / src

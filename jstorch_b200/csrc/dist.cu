@@ -3,14 +3,17 @@
 //
 // Row-sharded GEMM (configuration 5 of the benchmark):
 //   1. B is broadcast in place from the root (ncclBroadcast, NVLS where NCCL
-//      picks it);
-//   2. A_local and B are split once into hi / lo TF32 planes;
+//      picks it) on the communication stream, while the row blocks of A_local
+//      are split into hi / lo TF32 planes on the compute streams;
+//   2. B is split once it has arrived;
 //   3. for each row block of A_local the tensor-core kernel writes its C rows
-//      straight into their global place in C_full; an event hands the block
-//      to a communication stream that all-gathers it in place while the next
-//      block computes.  With block-cyclic row ownership (block i of rank r is
-//      global block i * nranks + r) the blocks of one round are contiguous in
-//      C_full, so each round is a single in-place ncclAllGather.
+//      straight into their global place in C_full (blocks alternate between two
+//      compute streams so the tail wave of one overlaps the next); an event
+//      hands the block to the communication stream, which all-gathers it in
+//      place while later blocks compute.  With block-cyclic row ownership
+//      (block i of rank r is global block i * nranks + r) the blocks of one
+//      round are contiguous in C_full, so each round is one in-place
+//      ncclAllGather.
 // No kernel reads another GPU's memory; all data moves through NCCL.
 //
 // Host-side failure handling: the communicator is created non-blocking and
@@ -26,22 +29,9 @@
 #include <thread>
 #include <vector>
 
-#include "../../include/jstorch_dist.h"
-#include "gemm_internal.h"
-
-struct jst_comm {
-    ncclComm_t nccl = nullptr;
-    int rank = 0;
-    int nranks = 1;
-    int device = 0;
-    double timeout_s = 60.0;
-    bool broken = false;
-    cudaStream_t comm_stream = nullptr;
-    std::vector<cudaEvent_t> events;
-};
+#include "dist_internal.h"
 
 namespace jst {
-namespace {
 
 int nccl_error(jst_comm* c, ncclResult_t r, const char* what) {
     char buf[256];
@@ -96,7 +86,6 @@ int ensure_events(jst_comm* c, size_t n) {
     return JST_OK;
 }
 
-}  // namespace
 }  // namespace jst
 
 extern "C" {
@@ -125,13 +114,16 @@ int jst_comm_init(jst_comm** out, int nranks, int rank, const unsigned char id[J
         delete c;
         return set_status(JST_ERR_NO_DEVICE, "no CUDA device");
     }
-    if (cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    if (cudaStreamCreateWithFlags(&c->comm_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&c->compute2, cudaStreamNonBlocking) != cudaSuccess) {
         cudaGetLastError();
+        if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
         delete c;
         return set_status(JST_ERR_CUDA, "stream create failed");
     }
     ncclUniqueId u;
     std::memcpy(&u, id, sizeof(u));
+    std::memcpy(c->id, id, JST_COMM_ID_BYTES);
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
     ncclResult_t r = ncclCommInitRankConfig(&c->nccl, nranks, u, rank, &cfg);
@@ -140,6 +132,7 @@ int jst_comm_init(jst_comm** out, int nranks, int rank, const unsigned char id[J
     if (rc) {
         if (c->nccl) ncclCommAbort(c->nccl);
         cudaStreamDestroy(c->comm_stream);
+        cudaStreamDestroy(c->compute2);
         delete c;
         return rc;
     }
@@ -183,6 +176,8 @@ int jst_comm_destroy(jst_comm* c) {
     using namespace jst;
     if (!c) return set_status(JST_OK, nullptr);
     int rc = JST_OK;
+    // buffers still registered are released first, while the barrier works
+    for (auto* sy : std::vector<jst_symm*>(c->symms)) jst_symm_free(sy);
     if (c->nccl) {
         if (c->broken) {
             ncclCommAbort(c->nccl);
@@ -197,7 +192,9 @@ int jst_comm_destroy(jst_comm* c) {
         }
     }
     for (auto e : c->events) cudaEventDestroy(e);
+    if (c->barrier_word) cudaFree(c->barrier_word);
     if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
+    if (c->compute2) cudaStreamDestroy(c->compute2);
     delete c;
     return rc ? rc : set_status(JST_OK, nullptr);
 }
@@ -212,51 +209,91 @@ int jst_gemm_rowsharded(jst_comm* c, const float* A_local, int M_local, int K, f
         return set_status(JST_ERR_ARG, "jst_gemm_rowsharded: bad argument");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int nchunks = M_local / chunk_rows;
-    rc = ensure_events(c, (size_t)nchunks + 1);
+    // events: entry, broadcast done, B split done, one per block, all done
+    rc = ensure_events(c, (size_t)nchunks + 4);
     if (rc) return rc;
+    cudaEvent_t ev_entry = c->events[0], ev_bcast = c->events[1], ev_bsplit = c->events[2],
+                ev_done = c->events[3];
+    auto ev_blk = [&](int i) { return c->events[4 + i]; };
+    auto cuda_ok = [&](cudaError_t e) {
+        if (e == cudaSuccess) return true;
+        cudaGetLastError();
+        rc = set_status(JST_ERR_CUDA, "stream / event hand-off failed");
+        return false;
+    };
+    // Row blocks alternate between the caller's stream and a second compute
+    // stream, so one block's last wave of tiles overlaps the next block's
+    // first; the collectives run in order on the communication stream.
+    cudaStream_t cs[2] = {s, c->compute2};
+    if (!cuda_ok(cudaEventRecord(ev_entry, s)) || !cuda_ok(cudaStreamWaitEvent(c->compute2, ev_entry, 0)) ||
+        !cuda_ok(cudaStreamWaitEvent(c->comm_stream, ev_entry, 0)))
+        return rc;
 
-    // 1. B from the root to every rank, in place, on the compute stream
-    rc = nccl_settle(c, ncclBroadcast(B, B, (size_t)K * N, ncclFloat, root, c->nccl, s), "ncclBroadcast(B)");
+    // 1. B from the root to every rank, in place, on the communication stream
+    rc = nccl_settle(c, ncclBroadcast(B, B, (size_t)K * N, ncclFloat, root, c->nccl, c->comm_stream),
+                     "ncclBroadcast(B)");
     if (rc) return rc;
-    if (M_local == 0) return set_status(JST_OK, nullptr);
+    if (!cuda_ok(cudaEventRecord(ev_bcast, c->comm_stream))) return rc;
 
-    // 2. split planes of A_local and B, once
     const size_t Kp = (size_t)((K + 3) & ~3);
     const size_t a_plane = (size_t)M_local * Kp, b_plane = (size_t)N * Kp;
     void* ws = nullptr;
-    rc = workspace_alloc((2 * a_plane + 2 * b_plane) * sizeof(float), s, &ws);
-    if (rc) return rc;
+    if (M_local > 0) {
+        rc = workspace_alloc((2 * a_plane + 2 * b_plane) * sizeof(float), s, &ws);
+        if (rc) return rc;
+        if (!cuda_ok(cudaEventRecord(ev_entry, s)) || !cuda_ok(cudaStreamWaitEvent(c->compute2, ev_entry, 0))) {
+            workspace_free(ws, s);
+            return rc;
+        }
+    }
     float* a_hi = static_cast<float*>(ws);
     float* a_lo = a_hi + a_plane;
     float* b_hi = a_lo + a_plane;
     float* b_lo = b_hi + b_plane;
-    rc = tc_split(A_local, 1, K, 0, M_local, K, 1, a_hi, a_lo, s);
-    if (!rc) rc = tc_split(B, 0, N, 0, N, K, 1, b_hi, b_lo, s);
 
-    // 3. per row block: GEMM into C_full, then its in-place all-gather on the comm stream
+    // 2. split each block of A_local on its own stream (overlaps the broadcast)
+    for (int i = 0; i < nchunks && !rc; ++i)
+        rc = tc_split(A_local + (size_t)i * chunk_rows * K, 1, K, 0, chunk_rows, K, 1, a_hi + (size_t)i * chunk_rows * Kp,
+                      a_lo + (size_t)i * chunk_rows * Kp, cs[i & 1]);
+    // 3. split B once it has arrived; both compute streams wait for it
+    if (!rc && nchunks > 0) {
+        if (cuda_ok(cudaStreamWaitEvent(s, ev_bcast, 0))) rc = tc_split(B, 0, N, 0, N, K, 1, b_hi, b_lo, s);
+        if (!rc && cuda_ok(cudaEventRecord(ev_bsplit, s))) cuda_ok(cudaStreamWaitEvent(c->compute2, ev_bsplit, 0));
+    }
+    // 4. per block: GEMM into its place in C_full, then its in-place
+    // all-gather -- or, with a multicast-backed C_full, the GEMM's epilogue
+    // stores the block once through the multicast view into every rank's copy
+    jst_symm* sy = find_symm(c, C_full, (size_t)M_local * c->nranks * N * sizeof(float));
     for (int i = 0; i < nchunks && !rc; ++i) {
         const int64_t grow = ((int64_t)i * c->nranks + c->rank) * chunk_rows;  // first global row of the block
         float* cblk = C_full + grow * N;
+        float* cdst = sy ? symm_multicast_ptr(sy, symm_offset(sy, cblk)) : cblk;
         rc = tc_gemm_planes(a_hi + (size_t)i * chunk_rows * Kp, a_lo + (size_t)i * chunk_rows * Kp, b_hi, b_lo,
-                            chunk_rows, N, K, 1, cblk, N, 0, nullptr, 0, device_error_word(), s);
+                            chunk_rows, N, K, 1, cdst, N, 0, nullptr, 0, device_error_word(), cs[i & 1], sy ? 1 : 0);
         if (rc) break;
-        if (cudaEventRecord(c->events[i], s) != cudaSuccess || cudaStreamWaitEvent(c->comm_stream, c->events[i], 0) !=
-                                                                     cudaSuccess) {
-            cudaGetLastError();
-            rc = set_status(JST_ERR_CUDA, "event hand-off failed");
+        if (!cuda_ok(cudaEventRecord(ev_blk(i), cs[i & 1])) ||
+            !cuda_ok(cudaStreamWaitEvent(c->comm_stream, ev_blk(i), 0)))
             break;
-        }
+        if (sy) continue;
         float* round0 = C_full + (int64_t)i * c->nranks * chunk_rows * N;
         rc = nccl_settle(c, ncclAllGather(cblk, round0, (size_t)chunk_rows * N, ncclFloat, c->nccl, c->comm_stream),
                          "ncclAllGather(C)");
     }
-    // the compute stream continues once every all-gather is done
-    if (cudaEventRecord(c->events[nchunks], c->comm_stream) != cudaSuccess ||
-        cudaStreamWaitEvent(s, c->events[nchunks], 0) != cudaSuccess) {
-        cudaGetLastError();
-        if (!rc) rc = set_status(JST_ERR_CUDA, "event hand-off failed");
+    // fused path: every rank's blocks have landed everywhere once every rank
+    // has passed its last GEMM (a 1-float all-reduce after all blocks)
+    if (!rc && sy && nchunks > 0) {
+        if (!c->barrier_word && cudaMalloc(&c->barrier_word, sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            rc = set_status(JST_ERR_NOMEM, "barrier word allocation failed");
+        }
+        if (!rc)
+            rc = nccl_settle(c, ncclAllReduce(c->barrier_word, c->barrier_word, 1, ncclFloat, ncclSum, c->nccl,
+                                              c->comm_stream),
+                             "ncclAllReduce(barrier)");
     }
-    const int frc = workspace_free(ws, s);
+    // the caller's stream continues once every collective (hence every block) is done
+    if (cuda_ok(cudaEventRecord(ev_done, c->comm_stream))) cuda_ok(cudaStreamWaitEvent(s, ev_done, 0));
+    const int frc = ws ? workspace_free(ws, s) : JST_OK;
     if (rc) return rc;
     return frc ? frc : set_status(JST_OK, nullptr);
 }

@@ -41,9 +41,11 @@ int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s);
 int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows, int K, int batch, float* hi,
              float* lo, cudaStream_t s);
 // Tensor-core kernel alone on existing planes (A planes M rows, B planes N rows).
+// mc_store: C is the multicast view of a multicast-backed buffer; every tile
+// is stored once through it and reaches every GPU of the team.
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
-                   cudaStream_t s);
+                   cudaStream_t s, int mc_store = 0);
 
 // FFMA SIMT path (no workspace)
 int ffma_gemm_run(const GemmArgs& a, cudaStream_t s);

@@ -68,6 +68,7 @@ struct Params {
     int relu;
     int tiles_m, tiles_n;
     uint32_t* err;  // device error word
+    int mc_store;   // C is a multicast address: store with multimem.st (fused all-gather)
 };
 
 __device__ __forceinline__ float epi(float v, const float* bias, int col, int relu) {
@@ -205,12 +206,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                         v.y = epi(__uint_as_float(r[j + 1]), p.bias, col0 + j + 1, p.relu);
                         v.z = epi(__uint_as_float(r[j + 2]), p.bias, col0 + j + 2, p.relu);
                         v.w = epi(__uint_as_float(r[j + 3]), p.bias, col0 + j + 3, p.relu);
-                        *reinterpret_cast<float4*>(crow + col0 + j) = v;
+                        if (p.mc_store) ptx::multimem_st_v4(crow + col0 + j, v);
+                        else *reinterpret_cast<float4*>(crow + col0 + j) = v;
                     }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (col0 + j < p.N) crow[col0 + j] = epi(__uint_as_float(r[j]), p.bias, col0 + j, p.relu);
+                    for (int j = 0; j < 32; ++j) {
+                        if (col0 + j >= p.N) continue;
+                        const float v = epi(__uint_as_float(r[j]), p.bias, col0 + j, p.relu);
+                        if (p.mc_store) ptx::multimem_st_f32(crow + col0 + j, v);
+                        else crow[col0 + j] = v;
+                    }
                 }
             }
         }
@@ -355,7 +361,7 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
 
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
-                   cudaStream_t s) {
+                   cudaStream_t s, int mc_store) {
     using namespace tc;
     const int Kp = (K + 3) & ~3;
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
@@ -379,6 +385,7 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
     p.tiles_m = (M + BM - 1) / BM;
     p.tiles_n = (N + BN - 1) / BN;
     p.err = err;
+    p.mc_store = mc_store;
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * batch;
     if (grid > 0x7fffffff) return set_status(JST_ERR_ARG, "tc: too many tiles");
     {

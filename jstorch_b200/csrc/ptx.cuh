@@ -158,6 +158,19 @@ __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- NVLink-switch stores
+// One store through a multicast virtual address reaches the same offset of
+// every GPU bound to the multicast object.  Weak stores: the kernel's
+// completion, followed by a cross-GPU barrier, publishes them.
+__device__ __forceinline__ void multimem_st_v4(float* addr, float4 v) {
+    asm volatile("multimem.st.weak.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void multimem_st_f32(float* addr, float v) {
+    asm volatile("multimem.st.weak.global.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
+}
+
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor (tcgen05 format, version 1) for a K-major
 // operand tile whose rows are `row_bytes` long and laid out with the matching

@@ -42,6 +42,10 @@ def load() -> ctypes.CDLL:
         d.jst_gemm_rowsharded.argtypes = [vp, vp, ci, ci, vp, ci, ci, vp, ci, vp]
         d.jst_bmm_batchsharded.restype = ci
         d.jst_bmm_batchsharded.argtypes = [vp, vp, vp, ci, ci, ci, ci, vp, vp]
+        d.jst_symm_alloc.restype = ci
+        d.jst_symm_alloc.argtypes = [vp, ctypes.c_size_t, ctypes.POINTER(vp), ctypes.POINTER(vp)]
+        d.jst_symm_free.restype = ci
+        d.jst_symm_free.argtypes = [vp]
         _dlib = d
     return _dlib
 
@@ -60,6 +64,42 @@ def row_plan(nranks: int, rank: int, m_local: int, chunk_rows: int) -> list[RowB
         raise ValueError("m_local must be a positive multiple of chunk_rows")
     return [RowBlock(i * chunk_rows, (i * nranks + rank) * chunk_rows, chunk_rows)
             for i in range(m_local // chunk_rows)]
+
+
+class _DeviceArray:
+    """Minimal __cuda_array_interface__ so torch can view library-owned memory."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class SymmBuffer:
+    """A multicast-backed buffer on every rank (jst_symm_alloc): a row-sharded
+    GEMM whose C lives here fuses its all-gather into the kernel epilogue."""
+
+    def __init__(self, comm: "Comm", nbytes: int):
+        h, p = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(load().jst_symm_alloc(comm.handle, nbytes, ctypes.byref(h), ctypes.byref(p)))
+        self.handle, self.ptr, self.nbytes = h, p.value, nbytes
+
+    def tensor(self, shape, dtype=None):
+        """A torch CUDA tensor viewing this rank's copy (no copy, fp32)."""
+        import torch
+
+        n = 1
+        for d in shape:
+            n *= d
+        if n * 4 > self.nbytes:
+            raise ValueError("shape exceeds the buffer")
+        return torch.as_tensor(_DeviceArray(self.ptr, tuple(shape)), device="cuda")
+
+    def free(self) -> None:
+        """Collective release (every rank, after its last use)."""
+        if self.handle:
+            rc = load().jst_symm_free(self.handle)
+            self.handle = None
+            _lib.check(rc)
 
 
 class Comm:
@@ -88,6 +128,10 @@ class Comm:
         obj = [cls.unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         return cls(world, rank, obj[0], timeout_s)
+
+    def symm_alloc(self, nbytes: int) -> SymmBuffer:
+        """Collective: a multicast-backed buffer of nbytes on every rank."""
+        return SymmBuffer(self, nbytes)
 
     def sync(self, stream) -> None:
         """Host wait for `stream`, bounded by the communicator deadline."""
