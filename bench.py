@@ -275,16 +275,26 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     comm = jdist.Comm.from_process_group(timeout_s=120.0)
     a = torch.from_numpy(a_host).to(dev)
     b = torch.from_numpy(b_host).to(dev)
-    # C in a multicast-backed buffer: the all-gather of C is fused into the
-    # GEMM epilogue (multimem stores through the NVLink switch)
-    symm, gather = None, "NCCL all-gather rounds overlapped with the next block"
-    if not args.nccl_allgather:
+    # how C reaches every rank (--c-gather):
+    #   copy       each block is pushed by the copy engines into the other
+    #              ranks' registered C (no SMs taken from the GEMM)
+    #   nccl       NCCL all-gather rounds overlapped with the next block
+    #   multicast  multimem stores in the GEMM epilogue to a multicast-backed C
+    symm, reg = None, None
+    gather = "NCCL all-gather rounds overlapped with the next block"
+    if args.c_gather == "multicast":
         try:
             symm = comm.symm_alloc(M * N * 4)
             gather = "fused into the GEMM epilogue (multimem stores to a multicast-backed C)"
         except _lib.JstError as e:
-            gather = f"NCCL all-gather rounds (multicast buffer unavailable: {e})"
+            gather += f" (multicast buffer unavailable: {e})"
     c = symm.tensor((M, N)) if symm else torch.empty((M, N), dtype=torch.float32, device=dev)
+    if args.c_gather == "copy":
+        try:
+            reg = comm.register(c)
+            gather = "copy-engine writes of each block into every other rank's registered C (CUDA IPC)"
+        except _lib.JstError as e:
+            gather += f" (registration unavailable: {e})"
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     flops = 2.0 * M * N * K
@@ -329,6 +339,14 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
     ms = float(tmax[0])
     value = flops / (ms * 1e-3) / 1e12
+
+    timeline = None
+    if args.trace:  # one extra step with the library's event timeline (not timed)
+        comm.trace(True)
+        step()
+        comm.sync(stream)
+        timeline = [(lab, round(ms, 3)) for lab, ms in comm.trace_read()]
+        comm.trace(False)
 
     # end to end: this rank's A rows (and B on the root) in from pinned host
     # memory, the sharded GEMM, this rank's C rows back to pinned host memory
@@ -391,6 +409,10 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
                    "l2": "inputs larger than L2 (A shard, B 256 MiB each per rank)"},
         "e2e": e2e, "roofline": roofline, "gpu_launches": int(tsum[1]), "clocks": clk,
     }
+    if timeline:
+        line["timeline_rank0"] = timeline
+    if reg:
+        reg.deregister()
     del c
     if symm:
         symm.free()
@@ -643,8 +665,10 @@ def main() -> None:
     ap.add_argument("--size", type=int, default=SIZE, help="square GEMM size at N=1 (default 8192)")
     ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
                     help="secondary measurement of one BASELINE configuration (0: the headline line)")
-    ap.add_argument("--nccl-allgather", action="store_true",
-                    help="N>1: gather C with NCCL all-gathers instead of the fused multicast epilogue")
+    ap.add_argument("--trace", action="store_true", help="N>1: add one traced step's timeline to the line")
+    ap.add_argument("--c-gather", choices=["copy", "nccl", "multicast"], default="copy",
+                    help="N>1: how C reaches every rank (copy engines into registered buffers, NCCL "
+                         "all-gathers, or multimem stores in the GEMM epilogue)")
     ap.add_argument("--chunk-rows", type=int, default=1024,
                     help="row block of the sharded GEMM at N>1 (its all-gather overlaps the next block)")
     args = ap.parse_args()

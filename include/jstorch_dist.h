@@ -40,6 +40,15 @@ int jst_comm_init(jst_comm** comm, int nranks, int rank, const unsigned char id[
 int jst_comm_sync(jst_comm* comm, jst_stream_t stream);
 int jst_comm_rank(const jst_comm* comm);
 int jst_comm_size(const jst_comm* comm);
+/*
+ * Timeline of the last row-sharded call (no counterpart in the reference):
+ * jst_comm_trace(comm, 1) turns event recording on; after the call and a
+ * jst_comm_sync, jst_comm_trace_read fills up to max_entries labels (each up
+ * to 31 chars + NUL, 32 bytes apart in `labels`) and millisecond offsets from
+ * the call's entry, and returns the number of entries.
+ */
+int jst_comm_trace(jst_comm* comm, int on);
+int jst_comm_trace_read(jst_comm* comm, char* labels, double* ms, int max_entries);
 /* Destroy (or, after an error, abort) the communicator and free its streams. */
 int jst_comm_destroy(jst_comm* comm);
 
@@ -58,6 +67,20 @@ int jst_symm_alloc(jst_comm* comm, size_t bytes, jst_symm** out, void** local);
 int jst_symm_free(jst_symm* buf);
 
 /*
+ * Register `bytes` of this rank's device memory at `ptr` with every rank
+ * (collective; CUDA IPC handles are exchanged through the communicator).  A
+ * row-sharded GEMM whose C_full lies in a registered buffer delivers each row
+ * block with copy-engine writes straight into the other ranks' buffers
+ * (no all-gather kernel, no SMs taken from the GEMM) and ends with one
+ * barrier.  The memory must come from cudaMalloc (directly or through a
+ * caching allocator) and stay allocated until jst_comm_deregister.
+ */
+typedef struct jst_reg jst_reg;
+int jst_comm_register(jst_comm* comm, void* ptr, size_t bytes, jst_reg** out);
+/* Collective: all ranks, after their last use of the buffer. */
+int jst_comm_deregister(jst_reg* reg);
+
+/*
  * Row-sharded C = A * B over all ranks (every rank receives the full C).
  *   A_local   [M_local, K] row-major on this rank: row block i (chunk_rows rows,
  *             i = 0 .. M_local/chunk_rows - 1) holds global rows
@@ -68,7 +91,9 @@ int jst_symm_free(jst_symm* buf);
  *   C_full    [M_local * nranks, N] on every rank.
  * Each row block is multiplied with the 3 x TF32 tensor-core kernel straight
  * into its place in C_full; its in-place all-gather runs on a second stream
- * while the next block is computed.  When C_full lies in a jst_symm buffer the
+ * while the next block is computed.  When C_full lies in a registered buffer
+ * (jst_comm_register) each block is instead copied by the copy engines into
+ * every other rank's buffer.  When C_full lies in a jst_symm buffer the
  * all-gather is fused into the GEMM instead: the kernel's epilogue stores each
  * tile once through the multicast address and the switch delivers it to every
  * rank (no collective for C, one barrier at the end).  Asynchronous on `stream`.

@@ -115,7 +115,7 @@ def build_core(force: bool = False, verbose: bool = False) -> Path:
     return CORE_EXT
 
 
-DIST_SOURCES = ["dist.cu", "symm.cu"]
+DIST_SOURCES = ["dist.cu", "symm.cu", "reg.cu"]
 DIST_LIB = PKG / "libjstorch_dist.so"
 
 

@@ -14,7 +14,9 @@
 //      (block i of rank r is global block i * nranks + r) the blocks of one
 //      round are contiguous in C_full, so each round is one in-place
 //      ncclAllGather.
-// No kernel reads another GPU's memory; all data moves through NCCL.
+// No kernel reads another GPU's memory.  C travels by NCCL all-gathers, by
+// copy-engine writes into registered peer buffers (jst_comm_register), or by
+// multimem stores into a multicast-backed buffer (jst_symm_alloc).
 //
 // Host-side failure handling: the communicator is created non-blocking and
 // every NCCL call is polled against a host deadline; on expiry the
@@ -23,6 +25,7 @@
 #include <cuda_runtime.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstdio>
 #include <cstring>
@@ -72,6 +75,22 @@ int ready(jst_comm* c) {
     if (cudaGetDevice(&dev) != cudaSuccess || dev != c->device)
         return set_status(JST_ERR_ARG, "current device differs from the communicator's device");
     return JST_OK;
+}
+
+void trace_mark(jst_comm* c, const char* label, cudaStream_t s) {
+    if (!c->trace) return;
+    if (c->trace_n == c->trace_ev.size()) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) {
+            cudaGetLastError();
+            return;
+        }
+        c->trace_ev.push_back(e);
+        c->trace_label.push_back(nullptr);
+    }
+    c->trace_label[c->trace_n] = label;
+    cudaEventRecord(c->trace_ev[c->trace_n], s);
+    ++c->trace_n;
 }
 
 int ensure_events(jst_comm* c, size_t n) {
@@ -169,6 +188,27 @@ int jst_comm_sync(jst_comm* c, jst_stream_t stream) {
     return set_status(JST_OK, nullptr);
 }
 
+int jst_comm_trace(jst_comm* c, int on) {
+    if (!c) return jst::set_status(JST_ERR_ARG, "null communicator");
+    c->trace = on != 0;
+    c->trace_n = 0;
+    return jst::set_status(JST_OK, nullptr);
+}
+
+int jst_comm_trace_read(jst_comm* c, char* labels, double* ms, int max_entries) {
+    if (!c || !labels || !ms) return -jst::set_status(JST_ERR_ARG, "jst_comm_trace_read: bad argument");
+    const int n = (int)std::min<size_t>(c->trace_n, (size_t)max_entries);
+    for (int i = 0; i < n; ++i) {
+        float t = 0.f;
+        if (cudaEventSynchronize(c->trace_ev[i]) != cudaSuccess ||
+            cudaEventElapsedTime(&t, c->trace_ev[0], c->trace_ev[i]) != cudaSuccess)
+            cudaGetLastError();
+        std::snprintf(labels + 32 * i, 32, "%s", c->trace_label[i] ? c->trace_label[i] : "");
+        ms[i] = t;
+    }
+    return n;
+}
+
 int jst_comm_rank(const jst_comm* c) { return c ? c->rank : -1; }
 int jst_comm_size(const jst_comm* c) { return c ? c->nranks : -1; }
 
@@ -178,6 +218,7 @@ int jst_comm_destroy(jst_comm* c) {
     int rc = JST_OK;
     // buffers still registered are released first, while the barrier works
     for (auto* sy : std::vector<jst_symm*>(c->symms)) jst_symm_free(sy);
+    for (auto* r : std::vector<jst_reg*>(c->regs)) jst_comm_deregister(r);
     if (c->nccl) {
         if (c->broken) {
             ncclCommAbort(c->nccl);
@@ -195,6 +236,7 @@ int jst_comm_destroy(jst_comm* c) {
     if (c->barrier_word) cudaFree(c->barrier_word);
     if (c->comm_stream) cudaStreamDestroy(c->comm_stream);
     if (c->compute2) cudaStreamDestroy(c->compute2);
+    for (auto st : c->copy_streams) cudaStreamDestroy(st);
     delete c;
     return rc ? rc : set_status(JST_OK, nullptr);
 }
@@ -209,8 +251,8 @@ int jst_gemm_rowsharded(jst_comm* c, const float* A_local, int M_local, int K, f
         return set_status(JST_ERR_ARG, "jst_gemm_rowsharded: bad argument");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     const int nchunks = M_local / chunk_rows;
-    // events: entry, broadcast done, B split done, one per block, all done
-    rc = ensure_events(c, (size_t)nchunks + 4);
+    // events: entry, broadcast done, B split done, all done, one per block, one per copy stream
+    rc = ensure_events(c, (size_t)nchunks + 4 + 8);
     if (rc) return rc;
     cudaEvent_t ev_entry = c->events[0], ev_bcast = c->events[1], ev_bsplit = c->events[2],
                 ev_done = c->events[3];
@@ -225,6 +267,8 @@ int jst_gemm_rowsharded(jst_comm* c, const float* A_local, int M_local, int K, f
     // stream, so one block's last wave of tiles overlaps the next block's
     // first; the collectives run in order on the communication stream.
     cudaStream_t cs[2] = {s, c->compute2};
+    c->trace_n = 0;
+    trace_mark(c, "entry", s);
     if (!cuda_ok(cudaEventRecord(ev_entry, s)) || !cuda_ok(cudaStreamWaitEvent(c->compute2, ev_entry, 0)) ||
         !cuda_ok(cudaStreamWaitEvent(c->comm_stream, ev_entry, 0)))
         return rc;
@@ -233,6 +277,7 @@ int jst_gemm_rowsharded(jst_comm* c, const float* A_local, int M_local, int K, f
     rc = nccl_settle(c, ncclBroadcast(B, B, (size_t)K * N, ncclFloat, root, c->nccl, c->comm_stream),
                      "ncclBroadcast(B)");
     if (rc) return rc;
+    trace_mark(c, "broadcast B done", c->comm_stream);
     if (!cuda_ok(cudaEventRecord(ev_bcast, c->comm_stream))) return rc;
 
     const size_t Kp = (size_t)((K + 3) & ~3);
@@ -258,12 +303,16 @@ int jst_gemm_rowsharded(jst_comm* c, const float* A_local, int M_local, int K, f
     // 3. split B once it has arrived; both compute streams wait for it
     if (!rc && nchunks > 0) {
         if (cuda_ok(cudaStreamWaitEvent(s, ev_bcast, 0))) rc = tc_split(B, 0, N, 0, N, K, 1, b_hi, b_lo, s);
+        trace_mark(c, "split B done", s);
         if (!rc && cuda_ok(cudaEventRecord(ev_bsplit, s))) cuda_ok(cudaStreamWaitEvent(c->compute2, ev_bsplit, 0));
     }
     // 4. per block: GEMM into its place in C_full, then its in-place
     // all-gather -- or, with a multicast-backed C_full, the GEMM's epilogue
     // stores the block once through the multicast view into every rank's copy
-    jst_symm* sy = find_symm(c, C_full, (size_t)M_local * c->nranks * N * sizeof(float));
+    const size_t c_bytes = (size_t)M_local * c->nranks * N * sizeof(float);
+    jst_symm* sy = find_symm(c, C_full, c_bytes);
+    jst_reg* reg = sy ? nullptr : find_reg(c, C_full, c_bytes);
+    const int ncopy = reg ? (int)std::min<size_t>(c->copy_streams.size(), 8) : 0;
     for (int i = 0; i < nchunks && !rc; ++i) {
         const int64_t grow = ((int64_t)i * c->nranks + c->rank) * chunk_rows;  // first global row of the block
         float* cblk = C_full + grow * N;
@@ -271,17 +320,37 @@ int jst_gemm_rowsharded(jst_comm* c, const float* A_local, int M_local, int K, f
         rc = tc_gemm_planes(a_hi + (size_t)i * chunk_rows * Kp, a_lo + (size_t)i * chunk_rows * Kp, b_hi, b_lo,
                             chunk_rows, N, K, 1, cdst, N, 0, nullptr, 0, device_error_word(), cs[i & 1], sy ? 1 : 0);
         if (rc) break;
+        trace_mark(c, "gemm block done", cs[i & 1]);
         if (!cuda_ok(cudaEventRecord(ev_blk(i), cs[i & 1])) ||
             !cuda_ok(cudaStreamWaitEvent(c->comm_stream, ev_blk(i), 0)))
             break;
         if (sy) continue;
+        if (reg) {  // copy engines push the block into every other rank's C_full
+            const size_t blk_bytes = (size_t)chunk_rows * N * sizeof(float);
+            for (int k = 1; k < c->nranks && !rc; ++k) {
+                const int q = (c->rank + k) % c->nranks;  // stagger destinations across ranks
+                cudaStream_t cp = c->copy_streams[(size_t)(k - 1) % ncopy];
+                if (!cuda_ok(cudaStreamWaitEvent(cp, ev_blk(i), 0))) break;
+                if (!cuda_ok(cudaMemcpyAsync(reg_peer_ptr(reg, q, cblk), cblk, blk_bytes, cudaMemcpyDeviceToDevice,
+                                             cp)))
+                    break;
+            }
+            continue;
+        }
         float* round0 = C_full + (int64_t)i * c->nranks * chunk_rows * N;
         rc = nccl_settle(c, ncclAllGather(cblk, round0, (size_t)chunk_rows * N, ncclFloat, c->nccl, c->comm_stream),
                          "ncclAllGather(C)");
+        trace_mark(c, "all-gather round done", c->comm_stream);
     }
-    // fused path: every rank's blocks have landed everywhere once every rank
-    // has passed its last GEMM (a 1-float all-reduce after all blocks)
-    if (!rc && sy && nchunks > 0) {
+    // copy path: the communication stream waits for every copy stream
+    for (int k = 0; k < ncopy && !rc; ++k) {
+        cudaEvent_t e = c->events[4 + (size_t)nchunks + k];
+        if (!cuda_ok(cudaEventRecord(e, c->copy_streams[k])) || !cuda_ok(cudaStreamWaitEvent(c->comm_stream, e, 0)))
+            break;
+    }
+    // fused and copy paths: every rank's blocks have landed everywhere once
+    // every rank has passed its last GEMM / copy (a 1-float all-reduce)
+    if (!rc && (sy || reg) && nchunks > 0) {
         if (!c->barrier_word && cudaMalloc(&c->barrier_word, sizeof(float)) != cudaSuccess) {
             cudaGetLastError();
             rc = set_status(JST_ERR_NOMEM, "barrier word allocation failed");
@@ -292,6 +361,7 @@ int jst_gemm_rowsharded(jst_comm* c, const float* A_local, int M_local, int K, f
                              "ncclAllReduce(barrier)");
     }
     // the caller's stream continues once every collective (hence every block) is done
+    trace_mark(c, "all done", c->comm_stream);
     if (cuda_ok(cudaEventRecord(ev_done, c->comm_stream))) cuda_ok(cudaStreamWaitEvent(s, ev_done, 0));
     const int frc = ws ? workspace_free(ws, s) : JST_OK;
     if (rc) return rc;

@@ -42,6 +42,14 @@ def load() -> ctypes.CDLL:
         d.jst_gemm_rowsharded.argtypes = [vp, vp, ci, ci, vp, ci, ci, vp, ci, vp]
         d.jst_bmm_batchsharded.restype = ci
         d.jst_bmm_batchsharded.argtypes = [vp, vp, vp, ci, ci, ci, ci, vp, vp]
+        d.jst_comm_trace.restype = ci
+        d.jst_comm_trace.argtypes = [vp, ci]
+        d.jst_comm_trace_read.restype = ci
+        d.jst_comm_trace_read.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double), ci]
+        d.jst_comm_register.restype = ci
+        d.jst_comm_register.argtypes = [vp, vp, ctypes.c_size_t, ctypes.POINTER(vp)]
+        d.jst_comm_deregister.restype = ci
+        d.jst_comm_deregister.argtypes = [vp]
         d.jst_symm_alloc.restype = ci
         d.jst_symm_alloc.argtypes = [vp, ctypes.c_size_t, ctypes.POINTER(vp), ctypes.POINTER(vp)]
         d.jst_symm_free.restype = ci
@@ -102,6 +110,25 @@ class SymmBuffer:
             _lib.check(rc)
 
 
+class Registration:
+    """A tensor registered with every rank (jst_comm_register)."""
+
+    def __init__(self, comm: "Comm", tensor):
+        if not tensor.is_contiguous():
+            raise ValueError("register a contiguous tensor")
+        h = ctypes.c_void_p()
+        _lib.check(load().jst_comm_register(comm.handle, tensor.data_ptr(), tensor.numel() * tensor.element_size(),
+                                            ctypes.byref(h)))
+        self.handle, self.tensor = h, tensor
+
+    def deregister(self) -> None:
+        """Collective (every rank, after its last use)."""
+        if self.handle:
+            rc = load().jst_comm_deregister(self.handle)
+            self.handle = None
+            _lib.check(rc)
+
+
 class Comm:
     """A rank's NCCL communicator (jst_comm) on the current CUDA device."""
 
@@ -129,6 +156,11 @@ class Comm:
         dist.broadcast_object_list(obj, src=0)
         return cls(world, rank, obj[0], timeout_s)
 
+    def register(self, tensor) -> "Registration":
+        """Collective: register a contiguous CUDA tensor with every rank so a
+        row-sharded GEMM into it delivers blocks by copy engine."""
+        return Registration(self, tensor)
+
     def symm_alloc(self, nbytes: int) -> SymmBuffer:
         """Collective: a multicast-backed buffer of nbytes on every rank."""
         return SymmBuffer(self, nbytes)
@@ -136,6 +168,19 @@ class Comm:
     def sync(self, stream) -> None:
         """Host wait for `stream`, bounded by the communicator deadline."""
         _lib.check(load().jst_comm_sync(self.handle, stream.cuda_stream))
+
+    def trace(self, on: bool = True) -> None:
+        """Record a timeline of the next row-sharded calls (see trace_read)."""
+        _lib.check(load().jst_comm_trace(self.handle, 1 if on else 0))
+
+    def trace_read(self) -> list[tuple[str, float]]:
+        """(label, ms since the call's entry) of the last traced row-sharded call."""
+        labels = ctypes.create_string_buffer(32 * 256)
+        ms = (ctypes.c_double * 256)()
+        n = load().jst_comm_trace_read(self.handle, labels, ms, 256)
+        if n < 0:
+            _lib.check(-n)
+        return [(labels.raw[32 * i:32 * i + 32].split(b"\0")[0].decode(), float(ms[i])) for i in range(n)]
 
     def destroy(self) -> None:
         if self.handle:

@@ -115,6 +115,18 @@ def gpu_sharded(rank: int, world: int, port: int, out_q) -> None:
         err2, _ = oracle.max_rel_err(A, B, cf.cpu().numpy(), oracle.gemm_f64(A, B))
         msgs.append(f"batchsharded err {err2:.2e}")
         ok = ok and err2 <= 2e-6
+        # copy-engine path: C registered with every rank
+        cr = torch.full((m_local * world, n), float("nan"), device="cuda")
+        reg = comm.register(cr)
+        try:
+            b.zero_() if rank != 0 else None
+            comm.gemm_rowsharded(a, b, cr, chunk, root=0, stream=st)
+            comm.sync(st)
+            err4, _ = oracle.max_rel_err(a_full, b_host, cr.cpu().numpy(), ref)
+            msgs.append(f"copy-engine err {err4:.2e}")
+            ok = ok and err4 <= 2e-6
+        finally:
+            reg.deregister()
         # fused path: C in a multicast-backed buffer, no all-gather collective
         buf = comm.symm_alloc(m_local * world * n * 4)
         try:
