@@ -280,21 +280,25 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     #              ranks' registered C (no SMs taken from the GEMM)
     #   nccl       NCCL all-gather rounds overlapped with the next block
     #   multicast  multimem stores in the GEMM epilogue to a multicast-backed C
+    #   auto       multicast where the devices support it, else copy, else nccl
     symm, reg = None, None
     gather = "NCCL all-gather rounds overlapped with the next block"
-    if args.c_gather == "multicast":
+    notes = []
+    if args.c_gather in ("multicast", "auto"):
         try:
             symm = comm.symm_alloc(M * N * 4)
             gather = "fused into the GEMM epilogue (multimem stores to a multicast-backed C)"
         except _lib.JstError as e:
-            gather += f" (multicast buffer unavailable: {e})"
+            notes.append(f"multicast buffer unavailable: {e}")
     c = symm.tensor((M, N)) if symm else torch.empty((M, N), dtype=torch.float32, device=dev)
-    if args.c_gather == "copy":
+    if args.c_gather == "copy" or (args.c_gather == "auto" and symm is None):
         try:
             reg = comm.register(c)
             gather = "copy-engine writes of each block into every other rank's registered C (CUDA IPC)"
         except _lib.JstError as e:
-            gather += f" (registration unavailable: {e})"
+            notes.append(f"registration unavailable: {e}")
+    if notes:
+        gather += " (" + "; ".join(notes) + ")"
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     flops = 2.0 * M * N * K
@@ -666,7 +670,7 @@ def main() -> None:
     ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
                     help="secondary measurement of one BASELINE configuration (0: the headline line)")
     ap.add_argument("--trace", action="store_true", help="N>1: add one traced step's timeline to the line")
-    ap.add_argument("--c-gather", choices=["copy", "nccl", "multicast"], default="copy",
+    ap.add_argument("--c-gather", choices=["auto", "multicast", "copy", "nccl"], default="auto",
                     help="N>1: how C reaches every rank (copy engines into registered buffers, NCCL "
                          "all-gathers, or multimem stores in the GEMM epilogue)")
     ap.add_argument("--chunk-rows", type=int, default=1024,

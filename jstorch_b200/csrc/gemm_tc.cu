@@ -24,7 +24,8 @@
 //                              products) per slab and commits each slab back to
 //                              the producer
 //                  warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns,
-//                              fused bias / ReLU, direct stores to C
+//                              fused bias / ReLU, a shared-memory transpose,
+//                              then row-contiguous 128-byte stores to C
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -58,7 +59,13 @@ constexpr uint32_t A_TILE_BYTES = BM * BK * 4;  // 8 KiB
 constexpr uint32_t B_TILE_BYTES = BN * BK * 4;  // 16 KiB
 constexpr uint32_t STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;  // 48 KiB
 constexpr uint32_t RING_BYTES = STAGES * STAGE_BYTES;                  // 192 KiB
-constexpr uint32_t SMEM_BYTES = RING_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+// Epilogue staging: each of the 4 epilogue warps transposes its 32 x 32 fp32
+// block through shared memory (rows 36 floats apart: 16-byte aligned and
+// bank-conflict free for the float4 accesses) so that every store instruction
+// writes four full 128-byte row segments of C.
+constexpr int STG_LD = 36;
+constexpr uint32_t STG_BYTES = 4 * 32 * STG_LD * 4;  // 18 KiB
+constexpr uint32_t SMEM_BYTES = RING_BYTES + 1024 /*align slack*/ + 256 /*barriers*/ + STG_BYTES;
 
 struct Params {
     int M, N, K, batch;
@@ -182,9 +189,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const int row = m0 + q * 32 + lane;
         const bool row_ok = ok && row < p.M;
-        float* crow = p.C + (int64_t)bidx * p.strideC + (int64_t)row * p.ldc;
+        float* cbase = p.C + (int64_t)bidx * p.strideC;
+        float* crow = cbase + (int64_t)row * p.ldc;
         const bool vec = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                          ((p.strideC & 3) == 0);
+        float* stg = reinterpret_cast<float*>(smem + RING_BYTES + 256) + (warp - 2) * (32 * STG_LD);
         if (ok) {
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
@@ -195,10 +204,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ptx::tmem_ld_32x32b_x32(taddr + D_HI_COL, r);
                 ptx::tmem_ld_32x32b_x32(taddr + D_LO_COL, rl);
                 ptx::tmem_ld_wait();
-                if (!row_ok) continue;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(rl[j]));
-                if (vec && col0 + 32 <= p.N) {
+                if (vec && col0 + 32 <= p.N) {  // warp-uniform
+                    // thread `lane` holds row q*32+lane: stage it ...
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
                         float4 v;
@@ -206,10 +215,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                         v.y = epi(__uint_as_float(r[j + 1]), p.bias, col0 + j + 1, p.relu);
                         v.z = epi(__uint_as_float(r[j + 2]), p.bias, col0 + j + 2, p.relu);
                         v.w = epi(__uint_as_float(r[j + 3]), p.bias, col0 + j + 3, p.relu);
-                        if (p.mc_store) ptx::multimem_st_v4(crow + col0 + j, v);
-                        else *reinterpret_cast<float4*>(crow + col0 + j) = v;
+                        *reinterpret_cast<float4*>(stg + lane * STG_LD + j) = v;
                     }
-                } else {
+                    __syncwarp();
+                    // ... and store it back four rows x 128 bytes per instruction
+#pragma unroll
+                    for (int it = 0; it < 8; ++it) {
+                        const int rr = it * 4 + (lane >> 3);
+                        const int cc = (lane & 7) * 4;
+                        const float4 v = *reinterpret_cast<const float4*>(stg + rr * STG_LD + cc);
+                        const int grow = m0 + q * 32 + rr;
+                        if (grow < p.M) {
+                            float* dst = cbase + (int64_t)grow * p.ldc + col0 + cc;
+                            if (p.mc_store) ptx::multimem_st_v4(dst, v);
+                            else *reinterpret_cast<float4*>(dst) = v;
+                        }
+                    }
+                    __syncwarp();  // the staging tile is rewritten by the next chunk
+                } else if (row_ok) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         if (col0 + j >= p.N) continue;
