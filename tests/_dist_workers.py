@@ -88,7 +88,8 @@ def gpu_sharded(rank: int, world: int, port: int, out_q) -> None:
         torch.cuda.set_device(rank)
         d = _init_pg(rank, world, port)
         comm = jdist.Comm.from_process_group(timeout_s=30.0)
-        m_local, k, n, chunk = 768, 320, 640, 256
+        # n = 1024: the multicast path sends B in 4 column panels of 256
+        m_local, k, n, chunk = 768, 320, 1024, 256
         plan = jdist.row_plan(world, rank, m_local, chunk)
         a_local = np.concatenate([synth.matrix(4, synth.A, blk.rows, k, "uniform", row0=blk.global_row0)
                                   for blk in plan])
