@@ -51,7 +51,10 @@ typedef enum jst_epilogue {
     JST_EPI_NONE = 0,
     JST_EPI_BIAS = 1,       /* C[i,j] = acc + bias[j]            */
     JST_EPI_RELU = 2,       /* C[i,j] = max(acc, 0)              */
-    JST_EPI_BIAS_RELU = 3   /* C[i,j] = max(acc + bias[j], 0)    */
+    JST_EPI_BIAS_RELU = 3,  /* C[i,j] = max(acc + bias[j], 0)    */
+    JST_EPI_MASK = 4        /* C[i,j] = acc * (aux[i,j] > 0 ? 1 : 0): the ReLU
+                               backward of the layer whose output is aux, fused
+                               into the GEMM that produces its upstream gradient */
 } jst_epilogue;
 
 typedef enum jst_kernel {
@@ -82,6 +85,8 @@ typedef struct jst_gemm_desc {
     int epilogue;              /* jst_epilogue                                    */
     int kernel;                /* jst_kernel                                      */
     jst_stream_t stream;
+    const float* aux;          /* JST_EPI_MASK: [batch][M][N] with ld_aux, stride_aux */
+    int64_t ld_aux; int64_t stride_aux;
 } jst_gemm_desc;
 
 /* Fill a descriptor for a packed row-major C = A*B (NN, batch 1, no epilogue). */
@@ -130,8 +135,10 @@ void launch_linear(const float* x, const float* w, const float* bias, float* out
  * README.md:37-84 of the reference documents torch.matmul(a, b, M, K, N) on
  * row-major Float32Array returning a Float32Array; the code base never
  * implemented it.  This is the native entry point an N-API shim binds: HOST
- * pointers in and out, staged through cached pinned buffers, computed on the
- * current device, synchronous on return.  c must hold M*N floats.
+ * pointers in and out (pageable or pinned), device buffers cached per device,
+ * computed on the current device, synchronous on return.  Large products are
+ * moved in row chunks so that the host->device copies, the GEMM and the
+ * device->host copy overlap.  c must hold M*N floats.
  */
 int jst_matmul_host(const float* a, const float* b, float* c, int M, int K, int N);
 

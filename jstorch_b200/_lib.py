@@ -19,7 +19,7 @@ STATUS_NAMES = {
     0: "JST_OK", 1: "JST_ERR_ARG", 2: "JST_ERR_ALIGN", 3: "JST_ERR_CUDA", 4: "JST_ERR_NCCL",
     5: "JST_ERR_TIMEOUT", 6: "JST_ERR_UNSUPPORTED", 7: "JST_ERR_NOMEM", 8: "JST_ERR_NO_DEVICE",
 }
-EPI_NONE, EPI_BIAS, EPI_RELU, EPI_BIAS_RELU = 0, 1, 2, 3
+EPI_NONE, EPI_BIAS, EPI_RELU, EPI_BIAS_RELU, EPI_MASK = 0, 1, 2, 3, 4
 KERNEL_AUTO, KERNEL_TC3XTF32, KERNEL_FFMA = 0, 1, 2
 KERNELS = {"auto": KERNEL_AUTO, "tc3xtf32": KERNEL_TC3XTF32, "ffma": KERNEL_FFMA}
 
@@ -45,6 +45,7 @@ class GemmDesc(ctypes.Structure):
         ("epilogue", ctypes.c_int),
         ("kernel", ctypes.c_int),
         ("stream", ctypes.c_void_p),
+        ("aux", ctypes.c_void_p), ("ld_aux", ctypes.c_int64), ("stride_aux", ctypes.c_int64),
     ]
 
 

@@ -8,6 +8,7 @@
 #include <pybind11/stl.h>
 
 #include "autograd.h"
+#include "compiled.h"
 #include "core_kernels.h"
 
 namespace py = pybind11;
@@ -107,6 +108,27 @@ PYBIND11_MODULE(_core, m) {
                 GradTensor::backward(self.shared_from_this(), u);
             }, py::arg("upstream") = py::none())
         .def("zero_grad", [](GradTensor& g) { g.grad_.reset(); g.has_grad = false; });
+
+    // CompiledGraph -- napi.cpp:1488-1830 (slot builders :1562-1574, run :1785).  run() here
+    // takes (input, params) and returns (output, [grad per param]); the reference's
+    // target / Adam arguments belong to its optimizer, which is not on this path.
+    py::class_<jst::core::CompiledGraph>(m, "CompiledGraph")
+        .def(py::init<>())
+        .def("input", &jst::core::CompiledGraph::input)
+        .def("param", &jst::core::CompiledGraph::param)
+        .def("matmul", &jst::core::CompiledGraph::matmul)
+        .def("transpose", &jst::core::CompiledGraph::transpose)
+        .def("add", &jst::core::CompiledGraph::add)
+        .def("relu", &jst::core::CompiledGraph::relu)
+        .def("setOutput", &jst::core::CompiledGraph::set_output)
+        .def("run", [](jst::core::CompiledGraph& g, const Tensor& x, const std::vector<Tensor>& params) {
+                std::vector<Tensor> grads;
+                Tensor y = g.run(x, params, grads);
+                return py::make_tuple(y, grads);
+            })
+        .def_property_readonly("fused", &jst::core::CompiledGraph::fused)
+        .def_property_readonly("replaying", &jst::core::CompiledGraph::replaying)
+        .def_property_readonly("kernelsPerRun", &jst::core::CompiledGraph::kernels_per_run);
 
     m.def("clearCache", &jst::core::clear_cache, "synchronise and drop cached device blocks (napi.cpp:755)");
     m.def("reservedBytes", &jst::core::reserved_bytes);

@@ -109,8 +109,9 @@ static int validate(const jst_gemm_desc* d, GemmArgs* a) {
     if (d->batch < 1) return set_status(JST_ERR_ARG, "batch must be >= 1");
     if (d->transA != 0 && d->transA != 1) return set_status(JST_ERR_ARG, "transA must be 0 or 1");
     if (d->transB != 0 && d->transB != 1) return set_status(JST_ERR_ARG, "transB must be 0 or 1");
-    if (d->epilogue < JST_EPI_NONE || d->epilogue > JST_EPI_BIAS_RELU)
-        return set_status(JST_ERR_ARG, "unknown epilogue");
+    if (d->epilogue < JST_EPI_NONE || d->epilogue > JST_EPI_MASK) return set_status(JST_ERR_ARG, "unknown epilogue");
+    if (d->epilogue == JST_EPI_MASK && (!d->aux || d->ld_aux < d->N || (d->batch > 1 && d->stride_aux < 0)))
+        return set_status(JST_ERR_ARG, "mask epilogue needs aux with ld_aux >= N");
     if (d->kernel < JST_KERNEL_AUTO || d->kernel > JST_KERNEL_FFMA) return set_status(JST_ERR_ARG, "unknown kernel");
     const bool has_bias = d->epilogue == JST_EPI_BIAS || d->epilogue == JST_EPI_BIAS_RELU;
     if (has_bias && !d->bias) return set_status(JST_ERR_ARG, "bias epilogue without a bias pointer");
@@ -136,6 +137,9 @@ static int validate(const jst_gemm_desc* d, GemmArgs* a) {
     a->C = d->C; a->ldc = d->ldc; a->strideC = d->strideC;
     a->bias = has_bias ? d->bias : nullptr;
     a->relu = (d->epilogue == JST_EPI_RELU || d->epilogue == JST_EPI_BIAS_RELU) ? 1 : 0;
+    a->aux = d->epilogue == JST_EPI_MASK ? d->aux : nullptr;
+    a->ld_aux = d->ld_aux;
+    a->stride_aux = d->stride_aux;
     return JST_OK;
 }
 
@@ -145,7 +149,14 @@ int workspace_alloc(size_t bytes, cudaStream_t s, void** out) {
     int dev = 0;
     int rc = current_device(&dev);
     if (rc) return rc;
-    return cuda_status(cudaMallocFromPoolAsync(out, bytes ? bytes : 16, g_dev[dev].pool, s), "workspace allocation");
+    if (!bytes) bytes = 16;
+    // Inside a stream capture the allocation becomes a graph memory node of the
+    // graph's own pool; outside, it comes from this library's pool.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    rc = cuda_status(cudaStreamIsCapturing(s, &cs), "capture query");
+    if (rc) return rc;
+    if (cs == cudaStreamCaptureStatusActive) return cuda_status(cudaMallocAsync(out, bytes, s), "workspace allocation");
+    return cuda_status(cudaMallocFromPoolAsync(out, bytes, g_dev[dev].pool, s), "workspace allocation");
 }
 
 int workspace_free(void* p, cudaStream_t s) { return cuda_status(cudaFreeAsync(p, s), "workspace release"); }
@@ -171,12 +182,12 @@ static int gemm(const jst_gemm_desc* d) {
     // tensor-core path: stream-ordered workspace from this library's pool
     const size_t bytes = tc_workspace_bytes(a);
     void* ws = nullptr;
-    rc = cuda_status(cudaMallocFromPoolAsync(&ws, bytes, g_dev[dev].pool, s), "workspace allocation");
+    rc = workspace_alloc(bytes, s, &ws);
     if (rc) return rc;
     rc = tc_gemm_run(a, ws, s);
-    cudaError_t fe = cudaFreeAsync(ws, s);
+    const int frc = workspace_free(ws, s);
     if (rc) return rc;
-    rc = cuda_status(fe, "workspace release");
+    rc = frc;
     return rc ? rc : set_status(JST_OK, nullptr);
 }
 

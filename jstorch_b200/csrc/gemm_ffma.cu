@@ -30,6 +30,8 @@ struct Params {
     float* C; int64_t ldc, strideC;
     const float* bias;
     int relu;
+    const float* aux;
+    int64_t ld_aux, stride_aux;
     int vecA, vecB, vecC;
 };
 
@@ -188,6 +190,7 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
             const int row = m0 + ty * 4 + r * (BM / RM) + i;
             if (row >= p.M) continue;
             float* crow = C + (int64_t)row * p.ldc;
+            const float* arow = p.aux ? p.aux + (int64_t)b * p.stride_aux + (int64_t)row * p.ld_aux : nullptr;
 #pragma unroll
             for (int c = 0; c < RN; ++c) {
                 const int col = n0 + tx * 4 + c * (BN / RN);
@@ -197,6 +200,7 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
                     float x = acc[r * 4 + i][c * 4 + j];
                     if (p.bias && col + j < p.N) x += __ldg(p.bias + col + j);
                     if (p.relu) x = fmaxf(x, 0.0f);
+                    if (arow && col + j < p.N && !(__ldg(arow + col + j) > 0.0f)) x = 0.0f;
                     v[j] = x;
                 }
                 if (p.vecC && col + 3 < p.N) {
@@ -234,6 +238,7 @@ int ffma_gemm_run(const GemmArgs& a, cudaStream_t s) {
     p.B = a.B; p.ldb = a.ldb; p.strideB = a.strideB;
     p.C = a.C; p.ldc = a.ldc; p.strideC = a.strideC;
     p.bias = a.bias; p.relu = a.relu;
+    p.aux = a.aux; p.ld_aux = a.ld_aux; p.stride_aux = a.stride_aux;
     p.vecA = aligned16(a.A) && (a.lda % 4 == 0) && (a.strideA % 4 == 0);
     p.vecB = aligned16(a.B) && (a.ldb % 4 == 0) && (a.strideB % 4 == 0);
     p.vecC = aligned16(a.C) && (a.ldc % 4 == 0) && (a.strideC % 4 == 0);

@@ -18,6 +18,8 @@ struct GemmArgs {
     float* C; int64_t ldc, strideC;
     const float* bias;
     int relu;
+    const float* aux;  // JST_EPI_MASK: C *= (aux > 0)
+    int64_t ld_aux, stride_aux;
 };
 
 // Check a public descriptor and normalise it into `a` (no device work).
@@ -45,7 +47,8 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
 // is stored once through it and reaches every GPU of the team.
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
-                   cudaStream_t s, int mc_store = 0);
+                   cudaStream_t s, int mc_store = 0, const float* aux = nullptr, int64_t ld_aux = 0,
+                   int64_t stride_aux = 0);
 
 // FFMA SIMT path (no workspace)
 int ffma_gemm_run(const GemmArgs& a, cudaStream_t s);

@@ -76,6 +76,8 @@ struct Params {
     int tiles_m, tiles_n;
     uint32_t* err;  // device error word
     int mc_store;   // C is a multicast address: store with multimem.st (fused all-gather)
+    const float* aux;  // mask epilogue: C *= (aux > 0)
+    int64_t ld_aux, stride_aux;
 };
 
 __device__ __forceinline__ float epi(float v, const float* bias, int col, int relu) {
@@ -206,6 +208,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ptx::tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(rl[j]));
+                const float* abase = p.aux ? p.aux + (int64_t)bidx * p.stride_aux : nullptr;
                 if (vec && col0 + 32 <= p.N) {  // warp-uniform
                     // thread `lane` holds row q*32+lane: stage it ...
 #pragma unroll
@@ -223,9 +226,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int it = 0; it < 8; ++it) {
                         const int rr = it * 4 + (lane >> 3);
                         const int cc = (lane & 7) * 4;
-                        const float4 v = *reinterpret_cast<const float4*>(stg + rr * STG_LD + cc);
+                        float4 v = *reinterpret_cast<const float4*>(stg + rr * STG_LD + cc);
                         const int grow = m0 + q * 32 + rr;
                         if (grow < p.M) {
+                            if (abase) {  // mask epilogue, read coalesced like the store
+                                const float* ar = abase + (int64_t)grow * p.ld_aux + col0 + cc;
+                                if (!(__ldg(ar + 0) > 0.0f)) v.x = 0.0f;
+                                if (!(__ldg(ar + 1) > 0.0f)) v.y = 0.0f;
+                                if (!(__ldg(ar + 2) > 0.0f)) v.z = 0.0f;
+                                if (!(__ldg(ar + 3) > 0.0f)) v.w = 0.0f;
+                            }
                             float* dst = cbase + (int64_t)grow * p.ldc + col0 + cc;
                             if (p.mc_store) ptx::multimem_st_v4(dst, v);
                             else *reinterpret_cast<float4*>(dst) = v;
@@ -236,7 +246,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         if (col0 + j >= p.N) continue;
-                        const float v = epi(__uint_as_float(r[j]), p.bias, col0 + j, p.relu);
+                        float v = epi(__uint_as_float(r[j]), p.bias, col0 + j, p.relu);
+                        if (abase && !(__ldg(abase + (int64_t)row * p.ld_aux + col0 + j) > 0.0f)) v = 0.0f;
                         if (p.mc_store) ptx::multimem_st_f32(crow + col0 + j, v);
                         else crow[col0 + j] = v;
                     }
@@ -384,7 +395,7 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
 
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
-                   cudaStream_t s, int mc_store) {
+                   cudaStream_t s, int mc_store, const float* aux, int64_t ld_aux, int64_t stride_aux) {
     using namespace tc;
     const int Kp = (K + 3) & ~3;
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
@@ -409,6 +420,9 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
     p.tiles_n = (N + BN - 1) / BN;
     p.err = err;
     p.mc_store = mc_store;
+    p.aux = aux;
+    p.ld_aux = ld_aux;
+    p.stride_aux = stride_aux;
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * batch;
     if (grid > 0x7fffffff) return set_status(JST_ERR_ARG, "tc: too many tiles");
     {
@@ -437,7 +451,7 @@ static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cud
     rc = tc_split(a.B, a.transB, a.ldb, a.strideB, a.N, a.K, a.batch, b_hi, b_lo, s);
     if (rc) return rc;
     return tc_gemm_planes(a_hi, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, a.C, a.ldc, a.strideC, a.bias, a.relu, err,
-                          s);
+                          s, 0, a.aux, a.ld_aux, a.stride_aux);
 }
 
 int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {

@@ -44,9 +44,11 @@ def _operand(x, name: str):
     raise ValueError(f"{name}: unsupported strides {tuple(x.stride())} for shape {tuple(x.shape)}")
 
 
-def gemm(a, b, out=None, *, bias=None, relu: bool = False, kernel: str = "auto", stream=None):
+def gemm(a, b, out=None, *, bias=None, relu: bool = False, mask=None, kernel: str = "auto", stream=None):
     """out = relu?(a @ b + bias) with a: [M,K] or [B,M,K], b: [K,N] or [B,K,N].
 
+    mask (a contiguous float32 tensor of out's shape) selects the ReLU-backward
+    epilogue instead: out = (a @ b) * (mask > 0); it excludes bias and relu.
     Transposed views of either operand are consumed in place (NT / TN forms).
     Runs asynchronously on `stream` (default: torch's current stream).
     """
@@ -68,6 +70,11 @@ def gemm(a, b, out=None, *, bias=None, relu: bool = False, kernel: str = "auto",
     if bias is not None:
         if bias.dtype != torch.float32 or bias.numel() != N or not bias.is_contiguous():
             raise ValueError("bias must be a contiguous float32 tensor with N elements")
+    if mask is not None:
+        if bias is not None or relu:
+            raise ValueError("mask excludes bias and relu")
+        if tuple(mask.shape) != shape or not mask.is_contiguous() or mask.dtype != torch.float32:
+            raise ValueError(f"mask must be a contiguous float32 tensor of shape {shape}")
     d = _lib.GemmDesc()
     d.transA, d.transB = ta, tb
     d.M, d.N, d.K = M, N, K
@@ -77,6 +84,9 @@ def gemm(a, b, out=None, *, bias=None, relu: bool = False, kernel: str = "auto",
     d.batch = batch
     d.bias = bias.data_ptr() if bias is not None else None
     d.epilogue = (_lib.EPI_BIAS if bias is not None else 0) | (_lib.EPI_RELU if relu else 0)
+    if mask is not None:
+        d.epilogue = _lib.EPI_MASK
+        d.aux, d.ld_aux, d.stride_aux = mask.data_ptr(), N, M * N
     d.kernel = _lib.KERNELS[kernel]
     st = stream if stream is not None else torch.cuda.current_stream(a.device)
     d.stream = st.cuda_stream
