@@ -280,7 +280,13 @@ Tensor CompiledGraph::run(const Tensor& input, const std::vector<Tensor>& params
             ck(cudaStreamEndCapture(stream_, &g), "end capture");
             size_t n = 0;
             cudaGraphGetNodes(g, nullptr, &n);
-            kernels_per_run_ = (int)n;
+            std::vector<cudaGraphNode_t> nodes(n);
+            if (n) cudaGraphGetNodes(g, nodes.data(), &n);
+            kernels_per_run_ = 0;
+            for (auto nd : nodes) {
+                cudaGraphNodeType t;
+                if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels_per_run_;
+            }
             const cudaError_t e = cudaGraphInstantiate(&exec_, g, 0);
             cudaGraphDestroy(g);
             ck(e, "graph instantiate");

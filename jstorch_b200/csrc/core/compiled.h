@@ -54,7 +54,7 @@ class CompiledGraph {
 
     bool fused() const { return fused_; }    // the tape was recognised as Linear layers
     bool replaying() const { return exec_ != nullptr; }
-    int kernels_per_run() const { return kernels_per_run_; }
+    int kernels_per_run() const { return kernels_per_run_; }  // kernel nodes of the captured graph
 
   private:
     struct Op {

@@ -1,7 +1,6 @@
 // gemm_ffma.cu -- fp32 FFMA (SIMT) GEMM for small and skinny shapes.
 //
-// Exact fp32 arithmetic (one fma per product, fp32 accumulation), no
-// workspace, all four layouts (op(A) = A or A^T, op(B) = B or B^T, the NN/NT/TN
+// Exact fp32 arithmetic (one fma per product, fp32 accumulation), all four layouts (op(A) = A or A^T, op(B) = B or B^T, the NN/NT/TN
 // forms of native/ops/matmul.cu:28-67 and of GradTensor::matmul_'s backward,
 // native/core/autograd.hpp:433-441), strided batches and the fused bias / ReLU
 // epilogue (matmul.cu:18-23, kernels.cuh:50).
@@ -14,8 +13,14 @@
 // while the current one is multiplied).  Global loads are float4 whenever
 // the operand's leading dimension and base allow it, scalar and bounds-checked
 // elsewhere.
+//
+// Split K: when the tiles of C cannot fill the SMs (the M = 256 layers of an
+// MLP, 512^3), K is cut into S slices of whole BK steps; CTA (tile, slice)
+// writes its partial tile to a stream-ordered workspace and a second kernel
+// adds the S partials in slice order (deterministic) and applies the epilogue.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "gemm_internal.h"
@@ -33,6 +38,8 @@ struct Params {
     const float* aux;
     int64_t ld_aux, stride_aux;
     int vecA, vecB, vecC;
+    int kslices, kchunk;  // split K: S slices of kchunk (a multiple of BK); S = 1: no split
+    float* part;          // S > 1: partial tiles, [S][batch][M][N] packed
 };
 
 // Two CTAs per SM: the register cap (128 for 256 threads) keeps 16 warps
@@ -57,7 +64,10 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
     const int ty = tid / TX;
     const int m0 = blockIdx.y * BM;
     const int n0 = blockIdx.x * BN;
-    const int b = blockIdx.z;
+    const int b = blockIdx.z / p.kslices;
+    const int slice = blockIdx.z - b * p.kslices;
+    const int kbeg = slice * p.kchunk;
+    const int kend = min(p.K, kbeg + p.kchunk);
     const float* A = p.A + (int64_t)b * p.strideA;
     const float* B = p.B + (int64_t)b * p.strideB;
     float* C = p.C + (int64_t)b * p.strideC;
@@ -151,15 +161,17 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
 #pragma unroll
         for (int j = 0; j < 4 * RN; ++j) acc[i][j] = 0.0f;
 
-    const int nk = (p.K + BK - 1) / BK;
+    // kbeg is a multiple of BK and slices end on a BK step or at K, so the
+    // bounds checks against K in fetch() also keep each slice to its own range
+    const int nk = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
     if (nk > 0) {
-        fetch(0);
+        fetch(kbeg);
         stash(0);
     }
     __syncthreads();
     for (int t = 0; t < nk; ++t) {
         const int buf = t & 1;
-        if (t + 1 < nk) fetch((t + 1) * BK);
+        if (t + 1 < nk) fetch(kbeg + (t + 1) * BK);
 #pragma unroll
         for (int k = 0; k < BK; ++k) {
             float a[4 * RM], bv[4 * RN];
@@ -180,6 +192,32 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
         }
         if (t + 1 < nk) stash(buf ^ 1);
         __syncthreads();
+    }
+
+    if (p.kslices > 1) {  // partial tile to the workspace; the reduce kernel applies the epilogue
+        float* P = p.part + ((int64_t)slice * (gridDim.z / p.kslices) + b) * ((int64_t)p.M * p.N);
+        const bool vec = (p.N & 3) == 0;
+#pragma unroll
+        for (int r = 0; r < RM; ++r)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int row = m0 + ty * 4 + r * (BM / RM) + i;
+                if (row >= p.M) continue;
+                float* prow = P + (int64_t)row * p.N;
+#pragma unroll
+                for (int c = 0; c < RN; ++c) {
+                    const int col = n0 + tx * 4 + c * (BN / RN);
+                    const float* v = &acc[r * 4 + i][c * 4];
+                    if (vec && col + 3 < p.N) {
+                        *reinterpret_cast<float4*>(prow + col) = make_float4(v[0], v[1], v[2], v[3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            if (col + j < p.N) prow[col + j] = v[j];
+                    }
+                }
+            }
+        return;
     }
 
     // epilogue: bias, ReLU, store
@@ -215,10 +253,57 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
     }
 }
 
+// C = epilogue(sum over s of part[s]), the slices added in order.  One thread
+// per 4 consecutive columns of a row.
+__global__ void splitk_reduce_kernel(const Params p, int batch) {
+    const int n4 = (p.N + 3) / 4;
+    const int64_t total = (int64_t)batch * p.M * n4;
+    const int64_t plane = (int64_t)batch * p.M * p.N;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int c4 = (int)(i % n4);
+        const int64_t br = i / n4;
+        const int row = (int)(br % p.M);
+        const int b = (int)(br / p.M);
+        const int col = c4 * 4;
+        const int64_t off = ((int64_t)b * p.M + row) * p.N + col;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const bool full = col + 3 < p.N && (p.N & 3) == 0;
+        for (int sl = 0; sl < p.kslices; ++sl) {
+            const float* src = p.part + sl * plane + off;
+            if (full) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(src));
+                v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (col + j < p.N) v[j] += __ldg(src + j);
+            }
+        }
+        float* crow = p.C + (int64_t)b * p.strideC + (int64_t)row * p.ldc;
+        const float* arow = p.aux ? p.aux + (int64_t)b * p.stride_aux + (int64_t)row * p.ld_aux : nullptr;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (col + j >= p.N) continue;
+            float x = v[j];
+            if (p.bias) x += __ldg(p.bias + col + j);
+            if (p.relu) x = fmaxf(x, 0.0f);
+            if (arow && !(__ldg(arow + col + j) > 0.0f)) x = 0.0f;
+            v[j] = x;
+        }
+        if (p.vecC && full) {
+            *reinterpret_cast<float4*>(crow + col) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (col + j < p.N) crow[col + j] = v[j];
+        }
+    }
+}
+
 template <int BM, int BN, int BK, int RM, int RN>
 static void launch_cfg(const Params& p, int batch, bool TA, bool TB, cudaStream_t s) {
     constexpr int threads = (BM / (4 * RM)) * (BN / (4 * RN));
-    dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, batch);
+    dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, batch * p.kslices);
     ProfScope prof(s, KID_FFMA_GEMM);
     if (!TA && !TB) ffma_gemm_kernel<BM, BN, BK, RM, RN, false, false><<<grid, threads, 0, s>>>(p);
     else if (!TA && TB) ffma_gemm_kernel<BM, BN, BK, RM, RN, false, true><<<grid, threads, 0, s>>>(p);
@@ -243,15 +328,68 @@ int ffma_gemm_run(const GemmArgs& a, cudaStream_t s) {
     p.vecB = aligned16(a.B) && (a.ldb % 4 == 0) && (a.strideB % 4 == 0);
     p.vecC = aligned16(a.C) && (a.ldc % 4 == 0) && (a.strideC % 4 == 0);
     if (a.batch > 65535) return set_status(JST_ERR_ARG, "ffma: batch > 65535");
+    p.kslices = 1;
+    p.kchunk = a.K;
+    p.part = nullptr;
     // Large tiles once there are enough of them to fill the 148 SMs; 64 x 64
     // tiles (4 x 4 per thread) otherwise.
     const long long big_tiles = (long long)((a.M + 127) / 128) * ((a.N + 127) / 128) * a.batch;
-    if (big_tiles >= 148)
+    if (big_tiles >= 148) {
         launch_cfg<128, 128, 8, 2, 2>(p, a.batch, a.transA, a.transB, s);
-    else
-        launch_cfg<64, 64, 16, 1, 1>(p, a.batch, a.transA, a.transB, s);
-    if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "ffma_gemm_kernel launch failed");
+        if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "ffma_gemm_kernel launch failed");
+        return JST_OK;
+    }
+    const SplitK sk = ffma_split_k(a);
+    p.kslices = sk.slices;
+    p.kchunk = sk.chunk;
+    void* ws = nullptr;
+    if (p.kslices > 1) {
+        const int rc = workspace_alloc(ffma_workspace_bytes(a), s, &ws);
+        if (rc) return rc;
+        p.part = static_cast<float*>(ws);
+    }
+    launch_cfg<64, 64, 16, 1, 1>(p, a.batch, a.transA, a.transB, s);
+    if (cudaPeekAtLastError() != cudaSuccess) {
+        if (ws) workspace_free(ws, s);
+        return set_status(JST_ERR_CUDA, "ffma_gemm_kernel launch failed");
+    }
+    if (p.kslices > 1) {
+        const int64_t total = (int64_t)a.batch * a.M * ((a.N + 3) / 4);
+        const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
+        {
+            ProfScope prof(s, KID_FFMA_GEMM);
+            splitk_reduce_kernel<<<blocks, 256, 0, s>>>(p, a.batch);
+        }
+        const cudaError_t le = cudaPeekAtLastError();
+        const int frc = workspace_free(ws, s);
+        if (le != cudaSuccess) return set_status(JST_ERR_CUDA, "split-K reduce launch failed");
+        if (frc) return frc;
+    }
     return JST_OK;
+}
+
+// Split K for the 64 x 64 configuration: enough (tile, slice) CTAs to fill
+// two per SM, slices of at least 64 along K, at most 16 slices.
+SplitK ffma_split_k(const GemmArgs& a) {
+    SplitK r{1, a.K};
+    const long long big_tiles = (long long)((a.M + 127) / 128) * ((a.N + 127) / 128) * a.batch;
+    if (big_tiles >= 148) return r;
+    const long long tiles = (long long)((a.M + 63) / 64) * ((a.N + 63) / 64) * a.batch;
+    const long long want = (2LL * 148 + tiles - 1) / tiles;
+    const long long kmax = a.K / 64;
+    long long S = std::min<long long>(std::min<long long>(want, kmax), 16);
+    if (S <= 1 || a.batch * S > 65535) return r;
+    int chunk = (int)((a.K + S - 1) / S);
+    chunk = (chunk + 15) / 16 * 16;  // whole BK = 16 steps
+    r.slices = (a.K + chunk - 1) / chunk;
+    r.chunk = chunk;
+    if (r.slices <= 1) r = SplitK{1, a.K};
+    return r;
+}
+
+size_t ffma_workspace_bytes(const GemmArgs& a) {
+    const SplitK sk = ffma_split_k(a);
+    return sk.slices > 1 ? (size_t)sk.slices * a.batch * a.M * a.N * sizeof(float) : 0;
 }
 
 // ------------------------------------------------------------ K == 0 fill

@@ -52,6 +52,12 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
 
 // FFMA SIMT path (no workspace)
 int ffma_gemm_run(const GemmArgs& a, cudaStream_t s);
+// split-K plan of the FFMA kernel (slices = 1: none) and its workspace size
+struct SplitK {
+    int slices, chunk;
+};
+SplitK ffma_split_k(const GemmArgs& a);
+size_t ffma_workspace_bytes(const GemmArgs& a);
 
 // K == 0: C = epilogue(0)
 int fill_epilogue_run(const GemmArgs& a, cudaStream_t s);

@@ -133,8 +133,9 @@ def test_compiled_config2_matches_eager_and_oracle(core):
         for l in range(3):
             assert rel(grads[2 * l].toArray(), ref["dW"][l]) < 1e-4
             assert rel(grads[2 * l + 1].toArray(), ref["db"][l]) < 1e-4
-    # forward + backward of 3 layers: 3 fwd GEMMs, 3 dW GEMMs, 2 dX GEMMs, 3 bias sums, input copy, seed copy
-    assert g.kernelsPerRun <= 14, g.kernelsPerRun
+    # 3 forward GEMMs, 3 dW GEMMs, 2 dX GEMMs, 3 bias sums, plus at most one
+    # split-K reduce per GEMM; no bias-add, ReLU or mask kernels
+    assert 11 <= g.kernelsPerRun <= 19, g.kernelsPerRun
 
 
 def test_compiled_new_input_values_and_batch(core):

@@ -223,3 +223,28 @@ def test_host_matmul_pipelined_chunks(jst, pinned):
     err, where = oracle.max_rel_err(A, B, C, ref, rows=rows)
     assert err <= TOL, (err, where)
     assert np.isfinite(C).all()
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False)])
+@pytest.mark.parametrize("M,N,K,batch", [(256, 1024, 1024, 1), (256, 10, 1024, 1), (10, 1024, 256, 1),
+                                         (512, 512, 512, 1), (100, 70, 999, 3), (64, 64, 130, 1)])
+def test_ffma_split_k(jst, ta, tb, M, N, K, batch):
+    """Shapes whose 64 x 64 tiles cannot fill the SMs run with K split into
+    slices and a fixed-order reduce: checked against the oracle with the
+    bias + ReLU epilogue, and bit-identical from run to run."""
+    import torch
+    rng = np.random.default_rng(M + 3 * N + 7 * K + batch)
+    A = _rand(rng, batch, M, K)
+    B = _rand(rng, batch, K, N)
+    bias = _rand(rng, N)
+    a = _dev(np.ascontiguousarray(A.transpose(0, 2, 1))).transpose(1, 2) if ta else _dev(A)
+    b = _dev(np.ascontiguousarray(B.transpose(0, 2, 1))).transpose(1, 2) if tb else _dev(B)
+    if batch == 1:
+        a, b = a[0], b[0]
+    c1 = jst.gemm(a, b, bias=_dev(bias), relu=True, kernel="ffma")
+    c2 = jst.gemm(a, b, bias=_dev(bias), relu=True, kernel="ffma")
+    torch.cuda.synchronize()
+    C1 = c1.cpu().numpy().reshape(batch, M, N)
+    np.testing.assert_array_equal(C1, c2.cpu().numpy().reshape(batch, M, N))
+    for i in range(batch):
+        _check(A[i], B[i], C1[i], bias=bias, relu=True)
