@@ -43,15 +43,21 @@ void gemm(cudaStream_t s, int transA, int transB, int M, int N, int K, const flo
 
 CompiledGraph::CompiledGraph() {
     ck(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "stream create");
+    ck(cudaStreamCreateWithFlags(&side_, cudaStreamNonBlocking), "stream create");
     ck(cudaEventCreateWithFlags(&ev_in_, cudaEventDisableTiming), "event create");
     ck(cudaEventCreateWithFlags(&ev_out_, cudaEventDisableTiming), "event create");
+    ck(cudaEventCreateWithFlags(&ev_side_, cudaEventDisableTiming), "event create");
 }
 
 CompiledGraph::~CompiledGraph() {
     if (stream_) cudaStreamSynchronize(stream_);
     if (exec_) cudaGraphExecDestroy(exec_);
+    if (side_) cudaStreamSynchronize(side_);
     if (ev_in_) cudaEventDestroy(ev_in_);
     if (ev_out_) cudaEventDestroy(ev_out_);
+    if (ev_side_) cudaEventDestroy(ev_side_);
+    for (auto e : ev_g_) cudaEventDestroy(e);
+    if (side_) cudaStreamDestroy(side_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -156,6 +162,11 @@ void CompiledGraph::alloc_buffers(int64_t batch) {
         g_.emplace_back(Shape{batch, L.out});
     }
     ones_ = Tensor::full({batch, layers_.back().out}, 1.0f);
+    while (ev_g_.size() < layers_.size()) {
+        cudaEvent_t e = nullptr;
+        ck(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event create");
+        ev_g_.push_back(e);
+    }
 }
 
 // forward + backward of the Linear chain on stream s (no host synchronisation,
@@ -178,10 +189,13 @@ void CompiledGraph::enqueue(cudaStream_t s, const std::vector<Tensor>& params) {
         const Layer& ly = layers_[l];
         const Tensor& x = l == 0 ? x_ : act_[l - 1];
         const float* g = (l == L - 1 && !last.relu) ? ones_.data() : g_[l].data();
+        // parameter gradients on the side stream, once g exists
+        ck(cudaEventRecord(ev_g_[l], s), "event record");
+        ck(cudaStreamWaitEvent(side_, ev_g_[l], 0), "stream wait");
         // dW [out, in] = g^T . x   (TN)
-        gemm(s, 1, 0, (int)ly.out, (int)ly.in, (int)B, g, ly.out, x.data(), ly.in, grads_[ly.w].data(), nullptr,
+        gemm(side_, 1, 0, (int)ly.out, (int)ly.in, (int)B, g, ly.out, x.data(), ly.in, grads_[ly.w].data(), nullptr,
              JST_EPI_NONE, nullptr);
-        if (ly.b >= 0) core::sum_rows(g, grads_[ly.b].data(), B, ly.out, s);
+        if (ly.b >= 0) core::sum_rows(g, grads_[ly.b].data(), B, ly.out, side_);
         // gradient of the previous layer's pre-activation: (g . W) masked by its ReLU (NN)
         if (l > 0) {
             const bool mask = layers_[l - 1].relu;
@@ -189,6 +203,8 @@ void CompiledGraph::enqueue(cudaStream_t s, const std::vector<Tensor>& params) {
                  nullptr, mask ? JST_EPI_MASK : JST_EPI_NONE, mask ? act_[l - 1].data() : nullptr);
         }
     }
+    ck(cudaEventRecord(ev_side_, side_), "event record");  // join
+    ck(cudaStreamWaitEvent(s, ev_side_, 0), "stream wait");
     ck(cudaPeekAtLastError(), "launch");
 }
 

@@ -11,6 +11,10 @@
 //   * backward per layer: dW = g^T . x (TN GEMM, straight into [out, in]),
 //     db = column sum of g, and the input gradient g . W (NN GEMM) with the
 //     previous layer's ReLU mask fused into its epilogue;
+//   * the weight / bias gradients of a layer run on a second stream, forked
+//     once the layer's upstream gradient exists and joined at the end, so the
+//     graph has two branches: the input-gradient chain and the parameter
+//     gradients that hang off it;
 //   * the first run executes eagerly (allocating every buffer), the second
 //     captures the whole pass into a CUDA graph, later runs replay it with one
 //     launch.  Buffers (activations, gradients) belong to the graph object.
@@ -86,8 +90,9 @@ class CompiledGraph {
     std::vector<Tensor> grads_; // parameter gradients
     Tensor ones_;
 
-    cudaStream_t stream_ = nullptr;
-    cudaEvent_t ev_in_ = nullptr, ev_out_ = nullptr;
+    cudaStream_t stream_ = nullptr, side_ = nullptr;
+    cudaEvent_t ev_in_ = nullptr, ev_out_ = nullptr, ev_side_ = nullptr;
+    std::vector<cudaEvent_t> ev_g_;  // per layer: its upstream gradient is ready
     cudaGraphExec_t exec_ = nullptr;
     std::vector<const float*> captured_params_;
     int runs_ = 0;
