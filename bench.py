@@ -570,6 +570,38 @@ def run_config(args) -> None:
                           stream)
         out.update({"metric": "config5 65536x8192x8192 GEMM on one GPU (strong-scaling reference point)",
                     "unit": "TFLOP/s", "value": flops / (ms * 1e-3) / 1e12, "ms": ms})
+    elif args.config == 6:
+        # host <-> device step either side of the path: Tensor.fromBuffer / toArray of a
+        # config-3 operand (256 MiB), against the reference's synchronous pageable copies
+        # (tensor.cpp:740-750, 775-800), restated with torch's pageable copy + synchronise
+        from jstorch_b200 import _core
+
+        A, _ = synth.config3()
+        flat = A.reshape(-1)
+        nbytes = flat.nbytes
+
+        def wall(fn):
+            for _ in range(max(args.warmup, 1)):
+                fn()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                fn()
+            torch.cuda.synchronize()
+            return (time.perf_counter() - t0) / args.steps
+
+        holder = {}
+        t_up = wall(lambda: holder.__setitem__("t", _core.Tensor.fromBuffer(flat)))
+        t_dn = wall(lambda: holder["t"].toFloat32Array())
+        dst = torch.empty(flat.size, dtype=torch.float32, device=dev)
+        src = torch.from_numpy(flat)
+        r_up = wall(lambda: (dst.copy_(src), torch.cuda.synchronize()))
+        r_dn = wall(lambda: dst.cpu())
+        gbs = lambda t: nbytes / t / 1e9
+        out.update({"metric": "host I/O: Tensor.fromBuffer / toFloat32Array of a 256 MiB operand", "unit": "GB/s",
+                    "value": gbs(t_up), "fromBuffer_gbs": gbs(t_up), "toArray_gbs": gbs(t_dn),
+                    "pageable_sync_reference_style": {"h2d_gbs": gbs(r_up), "d2h_gbs": gbs(r_dn)},
+                    "note": "wall clock per call incl. completion; pageable numpy source / destination"})
     print(json.dumps(out), flush=True)
 
 
@@ -684,7 +716,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--size", type=int, default=SIZE, help="square GEMM size at N=1 (default 8192)")
-    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5],
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5, 6],
                     help="secondary measurement of one BASELINE configuration (0: the headline line)")
     ap.add_argument("--trace", action="store_true", help="N>1: add one traced step's timeline to the line")
     ap.add_argument("--c-gather", choices=["auto", "multicast", "copy", "nccl"], default="auto",

@@ -77,9 +77,9 @@ def build_gemm(force: bool = False, ptxas_v: bool = False, verbose: bool = False
 
 
 CORE = CSRC / "core"
-CORE_CPP = ["tensor.cpp", "autograd.cpp", "allocator.cpp", "compiled.cpp", "binding.cpp"]
+CORE_CPP = ["tensor.cpp", "autograd.cpp", "allocator.cpp", "compiled.cpp", "hostio.cpp", "binding.cpp"]
 CORE_CU = ["kernels.cu"]
-CORE_HEADERS = ["tensor.h", "autograd.h", "allocator.h", "compiled.h", "core_kernels.h"]
+CORE_HEADERS = ["tensor.h", "autograd.h", "allocator.h", "compiled.h", "hostio.h", "core_kernels.h"]
 CORE_EXT = PKG / ("_core" + sysconfig.get_config_var("EXT_SUFFIX"))
 CXX = os.environ.get("CXX", "g++")
 

@@ -9,6 +9,7 @@
 
 #include "autograd.h"
 #include "compiled.h"
+#include "hostio.h"
 #include "core_kernels.h"
 
 namespace py = pybind11;
@@ -31,12 +32,19 @@ Tensor from_buffer(py::array_t<float, py::array::c_style | py::array::forcecast>
     return Tensor::from_buffer(a.data(), (int64_t)a.size(), s);
 }
 
-// toArray -- napi.cpp:235-238 returns nested JS arrays; here a numpy array of the tensor's shape
+// toArray -- napi.cpp:235-238 returns nested JS arrays; here a numpy array of
+// the tensor's shape, filled in place from the pinned staging
 py::array_t<float> to_array(const Tensor& t) {
-    std::vector<float> v = t.to_array();
     std::vector<py::ssize_t> shp(t.shape().begin(), t.shape().end());
     py::array_t<float> out(shp);
-    std::copy(v.begin(), v.end(), out.mutable_data());
+    t.to_host(out.mutable_data());
+    return out;
+}
+
+// toFloat32Array -- the flat Float32Array form (no nested arrays, napi.cpp:17-30)
+py::array_t<float> to_float32_array(const Tensor& t) {
+    py::array_t<float> out((py::ssize_t)t.size());
+    t.to_host(out.mutable_data());
     return out;
 }
 
@@ -63,6 +71,7 @@ PYBIND11_MODULE(_core, m) {
         .def("isContiguous", &Tensor::is_contiguous)
         .def("contiguous", &Tensor::contiguous)
         .def("toArray", &to_array)
+        .def("toFloat32Array", &to_float32_array)
         .def("data_ptr", [](const Tensor& t) { return reinterpret_cast<uintptr_t>(t.data()); })
         .def("matmul", &Tensor::matmul)
         .def("linear", [](const Tensor& x, const Tensor& w, const py::object& b) {
@@ -135,4 +144,5 @@ PYBIND11_MODULE(_core, m) {
     m.def("stridedCopies", &jst::core::strided_copy_count,
           "number of contiguous() materialisations (strided copies) so far");
     m.def("cachedBytes", &jst::core::cached_bytes);
+    m.def("releaseHostStaging", &jst::core::hostio_release, "free the pinned fromBuffer / toArray staging");
 }

@@ -81,10 +81,11 @@ __global__ void relu_backward_kernel(const float* __restrict__ g, const float* _
         out[i] = x[i] > 0.0f ? g[i] : 0.0f;
 }
 
-// One thread per column, rows split over blockDim.y warps-rows and combined in
-// shared memory: reads are coalesced along the columns.
+// One thread per column, rows split over blockDim.y (32) warp-rows and
+// combined in shared memory in a fixed order: reads are coalesced along the
+// columns, and a [256, N] gradient takes 8 loads per thread.
 __global__ void sum_rows_kernel(const float* __restrict__ a, float* __restrict__ out, int64_t rows, int64_t cols) {
-    __shared__ float part[8][33];
+    __shared__ float part[32][33];
     const int64_t col = blockIdx.x * 32 + threadIdx.x;
     float s = 0.0f;
     if (col < cols)
@@ -154,7 +155,7 @@ void relu_backward(const float* g, const float* x, float* out, int64_t n, cudaSt
 
 void sum_rows(const float* a, float* out, int64_t rows, int64_t cols, cudaStream_t s) {
     if (cols <= 0) return;
-    sum_rows_kernel<<<(unsigned)((cols + 31) / 32), dim3(32, 8), 0, s>>>(a, out, rows, cols);
+    sum_rows_kernel<<<(unsigned)((cols + 31) / 32), dim3(32, 32), 0, s>>>(a, out, rows, cols);
 }
 
 void randn(float* dst, int64_t n, uint64_t seed, cudaStream_t s) {

@@ -1,6 +1,8 @@
 // tensor.cpp -- host core Tensor (see tensor.h).
 #include "tensor.h"
 
+#include "hostio.h"
+
 #include <algorithm>
 #include <atomic>
 #include <numeric>
@@ -143,8 +145,7 @@ bool Tensor::is_contiguous() const {
 Tensor Tensor::from_buffer(const float* host, int64_t count, const Shape& shape) {
     if (numel(shape) != count) throw std::runtime_error("from_buffer: size mismatch");
     Tensor r(shape);
-    if (count)
-        check_cuda(cudaMemcpy(r.data(), host, (size_t)count * sizeof(float), cudaMemcpyHostToDevice), "H2D copy");
+    h2d(r.data(), host, count, g_stream);  // pinned, double-buffered staging (hostio.h)
     return r;
 }
 
@@ -164,11 +165,14 @@ Tensor Tensor::randn(const Shape& shape) {
 
 std::vector<float> Tensor::to_array() const {
     std::vector<float> out((size_t)size());
-    if (out.empty()) return out;
-    const Tensor c = contiguous();
-    check_cuda(cudaStreamSynchronize(g_stream), "synchronise");
-    check_cuda(cudaMemcpy(out.data(), c.data(), out.size() * sizeof(float), cudaMemcpyDeviceToHost), "D2H copy");
+    to_host(out.data());
     return out;
+}
+
+void Tensor::to_host(float* dst) const {
+    if (size() == 0) return;
+    const Tensor c = contiguous();  // strided views are gathered on the device first
+    d2h(dst, c.data(), c.size(), g_stream);  // waits for the core stream only
 }
 
 Tensor Tensor::contiguous() const {

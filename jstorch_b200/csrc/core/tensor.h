@@ -40,6 +40,8 @@ class Tensor {
 
     // host read-back honouring strides (tensor.cpp:775-800)
     std::vector<float> to_array() const;
+    // the same into a caller buffer of size() floats (a Float32Array's storage)
+    void to_host(float* dst) const;
 
     const Shape& shape() const { return shape_; }
     const Shape& strides() const { return strides_; }

@@ -254,49 +254,50 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
 }
 
 // C = epilogue(sum over s of part[s]), the slices added in order.  One thread
-// per 4 consecutive columns of a row.
+// per W consecutive columns of a row: W = 4 (float4 loads) when N % 4 == 0,
+// else W = 1.
+template <int W>
 __global__ void splitk_reduce_kernel(const Params p, int batch) {
-    const int n4 = (p.N + 3) / 4;
-    const int64_t total = (int64_t)batch * p.M * n4;
+    const int nw = p.N / W;
+    const int64_t total = (int64_t)batch * p.M * nw;
     const int64_t plane = (int64_t)batch * p.M * p.N;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int c4 = (int)(i % n4);
-        const int64_t br = i / n4;
+        const int cw = (int)(i % nw);
+        const int64_t br = i / nw;
         const int row = (int)(br % p.M);
         const int b = (int)(br / p.M);
-        const int col = c4 * 4;
+        const int col = cw * W;
         const int64_t off = ((int64_t)b * p.M + row) * p.N + col;
-        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const bool full = col + 3 < p.N && (p.N & 3) == 0;
+        float v[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[j] = 0.0f;
         for (int sl = 0; sl < p.kslices; ++sl) {
             const float* src = p.part + sl * plane + off;
-            if (full) {
+            if constexpr (W == 4) {
                 const float4 x = __ldg(reinterpret_cast<const float4*>(src));
                 v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w;
             } else {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (col + j < p.N) v[j] += __ldg(src + j);
+                v[0] += __ldg(src);
             }
         }
         float* crow = p.C + (int64_t)b * p.strideC + (int64_t)row * p.ldc;
         const float* arow = p.aux ? p.aux + (int64_t)b * p.stride_aux + (int64_t)row * p.ld_aux : nullptr;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            if (col + j >= p.N) continue;
+        for (int j = 0; j < W; ++j) {
             float x = v[j];
             if (p.bias) x += __ldg(p.bias + col + j);
             if (p.relu) x = fmaxf(x, 0.0f);
             if (arow && !(__ldg(arow + col + j) > 0.0f)) x = 0.0f;
             v[j] = x;
         }
-        if (p.vecC && full) {
-            *reinterpret_cast<float4*>(crow + col) = make_float4(v[0], v[1], v[2], v[3]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if (col + j < p.N) crow[col + j] = v[j];
+        if constexpr (W == 4) {
+            if (p.vecC) {
+                *reinterpret_cast<float4*>(crow + col) = make_float4(v[0], v[1], v[2], v[3]);
+                continue;
+            }
         }
+#pragma unroll
+        for (int j = 0; j < W; ++j) crow[col + j] = v[j];
     }
 }
 
@@ -354,11 +355,13 @@ int ffma_gemm_run(const GemmArgs& a, cudaStream_t s) {
         return set_status(JST_ERR_CUDA, "ffma_gemm_kernel launch failed");
     }
     if (p.kslices > 1) {
-        const int64_t total = (int64_t)a.batch * a.M * ((a.N + 3) / 4);
+        const bool w4 = (a.N & 3) == 0;
+        const int64_t total = (int64_t)a.batch * a.M * (w4 ? a.N / 4 : a.N);
         const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
         {
             ProfScope prof(s, KID_FFMA_GEMM);
-            splitk_reduce_kernel<<<blocks, 256, 0, s>>>(p, a.batch);
+            if (w4) splitk_reduce_kernel<4><<<blocks, 256, 0, s>>>(p, a.batch);
+            else splitk_reduce_kernel<1><<<blocks, 256, 0, s>>>(p, a.batch);
         }
         const cudaError_t le = cudaPeekAtLastError();
         const int frc = workspace_free(ws, s);
@@ -368,14 +371,15 @@ int ffma_gemm_run(const GemmArgs& a, cudaStream_t s) {
     return JST_OK;
 }
 
-// Split K for the 64 x 64 configuration: enough (tile, slice) CTAs to fill
-// two per SM, slices of at least 64 along K, at most 16 slices.
+// Split K for the 64 x 64 configuration: as many (tile, slice) CTAs as fit in
+// one wave at two per SM (a second, partial wave would cost a whole tile
+// time), slices of at least 64 along K, at most 16 slices.
 SplitK ffma_split_k(const GemmArgs& a) {
     SplitK r{1, a.K};
     const long long big_tiles = (long long)((a.M + 127) / 128) * ((a.N + 127) / 128) * a.batch;
     if (big_tiles >= 148) return r;
     const long long tiles = (long long)((a.M + 63) / 64) * ((a.N + 63) / 64) * a.batch;
-    const long long want = (2LL * 148 + tiles - 1) / tiles;
+    const long long want = 2LL * 148 / tiles;
     const long long kmax = a.K / 64;
     long long S = std::min<long long>(std::min<long long>(want, kmax), 16);
     if (S <= 1 || a.batch * S > 65535) return r;
