@@ -52,9 +52,12 @@ typedef enum jst_epilogue {
     JST_EPI_BIAS = 1,       /* C[i,j] = acc + bias[j]            */
     JST_EPI_RELU = 2,       /* C[i,j] = max(acc, 0)              */
     JST_EPI_BIAS_RELU = 3,  /* C[i,j] = max(acc + bias[j], 0)    */
-    JST_EPI_MASK = 4        /* C[i,j] = acc * (aux[i,j] > 0 ? 1 : 0): the ReLU
+    JST_EPI_MASK = 4,       /* C[i,j] = acc * (aux[i,j] > 0 ? 1 : 0): the ReLU
                                backward of the layer whose output is aux, fused
                                into the GEMM that produces its upstream gradient */
+    JST_EPI_BIAS_ROW = 8,   /* C[i,j] = acc + bias[i]  (bias [M]: one value per
+                               output channel of a convolution)              */
+    JST_EPI_BIAS_ROW_RELU = 10  /* C[i,j] = max(acc + bias[i], 0)            */
 } jst_epilogue;
 
 typedef enum jst_kernel {
@@ -81,7 +84,7 @@ typedef struct jst_gemm_desc {
     const float* B; int64_t ldb; int64_t strideB;
     float* C;       int64_t ldc; int64_t strideC;
     int batch;                 /* >= 1                                            */
-    const float* bias;         /* [N], required for the *_BIAS* epilogues         */
+    const float* bias;         /* [N] (or [M] for *_BIAS_ROW*), required for the bias epilogues */
     int epilogue;              /* jst_epilogue                                    */
     int kernel;                /* jst_kernel                                      */
     jst_stream_t stream;

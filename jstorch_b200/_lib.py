@@ -13,6 +13,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libjstorch_gemm.so"
 HEADER = PKG.parent / "include" / "jstorch_gemm.h"
+CONV_HEADER = PKG.parent / "include" / "jstorch_conv.h"
 
 JST_OK = 0
 STATUS_NAMES = {
@@ -20,6 +21,7 @@ STATUS_NAMES = {
     5: "JST_ERR_TIMEOUT", 6: "JST_ERR_UNSUPPORTED", 7: "JST_ERR_NOMEM", 8: "JST_ERR_NO_DEVICE",
 }
 EPI_NONE, EPI_BIAS, EPI_RELU, EPI_BIAS_RELU, EPI_MASK = 0, 1, 2, 3, 4
+EPI_BIAS_ROW, EPI_BIAS_ROW_RELU = 8, 10
 KERNEL_AUTO, KERNEL_TC3XTF32, KERNEL_FFMA = 0, 1, 2
 KERNELS = {"auto": KERNEL_AUTO, "tc3xtf32": KERNEL_TC3XTF32, "ffma": KERNEL_FFMA}
 
@@ -95,6 +97,21 @@ def load() -> ctypes.CDLL:
     lib.jst_profile_enable.argtypes = [ci]
     lib.jst_profile_read.restype = ci
     lib.jst_profile_read.argtypes = [ctypes.POINTER(KernelStat), ci]
+    # convolution launchers (include/jstorch_conv.h): 5 pointers, then ints, then the stream
+    conv1d_args = [vp] * 5 + [ci] * 10 + [vp]
+    conv2d_args = [vp] * 5 + [ci] * 16 + [vp]
+    for name in ("launch_conv1d", "launch_conv_transpose1d"):
+        getattr(lib, name).restype = None
+        getattr(lib, name).argtypes = conv1d_args
+    for name in ("launch_conv2d", "launch_conv_transpose2d"):
+        getattr(lib, name).restype = None
+        getattr(lib, name).argtypes = conv2d_args
+    for name in ("launch_conv1d_backward_weight", "launch_conv_transpose1d_backward_weight"):
+        getattr(lib, name).restype = None
+        getattr(lib, name).argtypes = [vp] * 4 + [ci] * 10 + [vp]
+    for name in ("launch_conv2d_backward_weight", "launch_conv_transpose2d_backward_weight"):
+        getattr(lib, name).restype = None
+        getattr(lib, name).argtypes = [vp] * 4 + [ci] * 16 + [vp]
     _lib = lib
     return lib
 
@@ -133,9 +150,9 @@ def check_last() -> None:
     check(load().jst_get_last_status())
 
 
-def header_functions() -> list[str]:
-    """Names of every function the public header declares."""
-    text = HEADER.read_text()
+def header_functions(header: Path = HEADER) -> list[str]:
+    """Names of every function a public header declares."""
+    text = header.read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][A-Za-z0-9_]*\s*\*?\s*([A-Za-z_][A-Za-z0-9_]*)\s*\(",
                        text, flags=re.M)

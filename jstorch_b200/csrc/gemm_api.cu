@@ -109,11 +109,14 @@ static int validate(const jst_gemm_desc* d, GemmArgs* a) {
     if (d->batch < 1) return set_status(JST_ERR_ARG, "batch must be >= 1");
     if (d->transA != 0 && d->transA != 1) return set_status(JST_ERR_ARG, "transA must be 0 or 1");
     if (d->transB != 0 && d->transB != 1) return set_status(JST_ERR_ARG, "transB must be 0 or 1");
-    if (d->epilogue < JST_EPI_NONE || d->epilogue > JST_EPI_MASK) return set_status(JST_ERR_ARG, "unknown epilogue");
+    const int e = d->epilogue;
+    if (!(e >= JST_EPI_NONE && e <= JST_EPI_MASK) && e != JST_EPI_BIAS_ROW && e != JST_EPI_BIAS_ROW_RELU)
+        return set_status(JST_ERR_ARG, "unknown epilogue");
     if (d->epilogue == JST_EPI_MASK && (!d->aux || d->ld_aux < d->N || (d->batch > 1 && d->stride_aux < 0)))
         return set_status(JST_ERR_ARG, "mask epilogue needs aux with ld_aux >= N");
     if (d->kernel < JST_KERNEL_AUTO || d->kernel > JST_KERNEL_FFMA) return set_status(JST_ERR_ARG, "unknown kernel");
-    const bool has_bias = d->epilogue == JST_EPI_BIAS || d->epilogue == JST_EPI_BIAS_RELU;
+    const bool row_bias = e == JST_EPI_BIAS_ROW || e == JST_EPI_BIAS_ROW_RELU;
+    const bool has_bias = e == JST_EPI_BIAS || e == JST_EPI_BIAS_RELU || row_bias;
     if (has_bias && !d->bias) return set_status(JST_ERR_ARG, "bias epilogue without a bias pointer");
     const int64_t a_rows = d->transA ? d->K : d->M, a_cols = d->transA ? d->M : d->K;
     const int64_t b_rows = d->transB ? d->N : d->K, b_cols = d->transB ? d->K : d->N;
@@ -136,7 +139,8 @@ static int validate(const jst_gemm_desc* d, GemmArgs* a) {
     a->B = d->B; a->ldb = d->ldb; a->strideB = d->strideB;
     a->C = d->C; a->ldc = d->ldc; a->strideC = d->strideC;
     a->bias = has_bias ? d->bias : nullptr;
-    a->relu = (d->epilogue == JST_EPI_RELU || d->epilogue == JST_EPI_BIAS_RELU) ? 1 : 0;
+    a->bias_row = row_bias ? 1 : 0;
+    a->relu = (e == JST_EPI_RELU || e == JST_EPI_BIAS_RELU || e == JST_EPI_BIAS_ROW_RELU) ? 1 : 0;
     a->aux = d->epilogue == JST_EPI_MASK ? d->aux : nullptr;
     a->ld_aux = d->ld_aux;
     a->stride_aux = d->stride_aux;

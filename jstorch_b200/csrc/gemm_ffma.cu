@@ -34,6 +34,7 @@ struct Params {
     const float* B; int64_t ldb, strideB;
     float* C; int64_t ldc, strideC;
     const float* bias;
+    int bias_row;  // bias[row] instead of bias[col]
     int relu;
     const float* aux;
     int64_t ld_aux, stride_aux;
@@ -236,7 +237,7 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     float x = acc[r * 4 + i][c * 4 + j];
-                    if (p.bias && col + j < p.N) x += __ldg(p.bias + col + j);
+                    if (p.bias && col + j < p.N) x += __ldg(p.bias + (p.bias_row ? row : col + j));
                     if (p.relu) x = fmaxf(x, 0.0f);
                     if (arow && col + j < p.N && !(__ldg(arow + col + j) > 0.0f)) x = 0.0f;
                     v[j] = x;
@@ -285,7 +286,7 @@ __global__ void splitk_reduce_kernel(const Params p, int batch) {
 #pragma unroll
         for (int j = 0; j < W; ++j) {
             float x = v[j];
-            if (p.bias) x += __ldg(p.bias + col + j);
+            if (p.bias) x += __ldg(p.bias + (p.bias_row ? row : col + j));
             if (p.relu) x = fmaxf(x, 0.0f);
             if (arow && !(__ldg(arow + col + j) > 0.0f)) x = 0.0f;
             v[j] = x;
@@ -323,7 +324,7 @@ int ffma_gemm_run(const GemmArgs& a, cudaStream_t s) {
     p.A = a.A; p.lda = a.lda; p.strideA = a.strideA;
     p.B = a.B; p.ldb = a.ldb; p.strideB = a.strideB;
     p.C = a.C; p.ldc = a.ldc; p.strideC = a.strideC;
-    p.bias = a.bias; p.relu = a.relu;
+    p.bias = a.bias; p.bias_row = a.bias_row; p.relu = a.relu;
     p.aux = a.aux; p.ld_aux = a.ld_aux; p.stride_aux = a.stride_aux;
     p.vecA = aligned16(a.A) && (a.lda % 4 == 0) && (a.strideA % 4 == 0);
     p.vecB = aligned16(a.B) && (a.ldb % 4 == 0) && (a.strideB % 4 == 0);
@@ -398,12 +399,12 @@ size_t ffma_workspace_bytes(const GemmArgs& a) {
 
 // ------------------------------------------------------------ K == 0 fill
 __global__ void fill_epilogue_kernel(float* C, int M, int N, int64_t ldc, int64_t strideC, const float* bias,
-                                     int relu) {
+                                     int bias_row, int relu) {
     const int b = blockIdx.z;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)M * N;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int r = (int)(i / N), c = (int)(i % N);
-        float v = bias ? bias[c] : 0.0f;
+        float v = bias ? bias[bias_row ? r : c] : 0.0f;
         if (relu) v = fmaxf(v, 0.0f);
         C[(int64_t)b * strideC + (int64_t)r * ldc + c] = v;
     }
@@ -414,7 +415,7 @@ int fill_epilogue_run(const GemmArgs& a, cudaStream_t s) {
     if (total == 0) return JST_OK;
     const int blocks = (int)((total + 255) / 256 < 1024 ? (total + 255) / 256 : 1024);
     ProfScope prof(s, KID_FILL);
-    fill_epilogue_kernel<<<dim3(blocks, 1, a.batch), 256, 0, s>>>(a.C, a.M, a.N, a.ldc, a.strideC, a.bias, a.relu);
+    fill_epilogue_kernel<<<dim3(blocks, 1, a.batch), 256, 0, s>>>(a.C, a.M, a.N, a.ldc, a.strideC, a.bias, a.bias_row, a.relu);
     if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "fill kernel launch failed");
     return JST_OK;
 }

@@ -17,6 +17,7 @@ struct GemmArgs {
     const float* B; int64_t ldb, strideB;
     float* C; int64_t ldc, strideC;
     const float* bias;
+    int bias_row;  // bias indexed by row (JST_EPI_BIAS_ROW*) instead of column
     int relu;
     const float* aux;  // JST_EPI_MASK: C *= (aux > 0)
     int64_t ld_aux, stride_aux;
@@ -48,7 +49,7 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
                    cudaStream_t s, int mc_store = 0, const float* aux = nullptr, int64_t ld_aux = 0,
-                   int64_t stride_aux = 0);
+                   int64_t stride_aux = 0, int bias_row = 0);
 
 // FFMA SIMT path (no workspace)
 int ffma_gemm_run(const GemmArgs& a, cudaStream_t s);
@@ -63,7 +64,15 @@ size_t ffma_workspace_bytes(const GemmArgs& a);
 int fill_epilogue_run(const GemmArgs& a, cudaStream_t s);
 
 // ---- launch accounting / optional event timing (profile.cu)
-enum KernelId { KID_TC_GEMM = 0, KID_SPLIT_ROWS, KID_SPLIT_TRANSPOSE, KID_FFMA_GEMM, KID_FILL, KERNEL_ID_COUNT };
+enum KernelId {
+    KID_TC_GEMM = 0,
+    KID_SPLIT_ROWS,
+    KID_SPLIT_TRANSPOSE,
+    KID_FFMA_GEMM,
+    KID_FILL,
+    KID_CONV,  // im2col / col2im / permute of the convolution launchers
+    KERNEL_ID_COUNT
+};
 
 // Construct immediately before a kernel launch and let it go out of scope
 // right after: counts the launch and, when profiling is on, brackets it with

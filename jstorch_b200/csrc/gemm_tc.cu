@@ -72,6 +72,7 @@ struct Params {
     float* C;
     int64_t ldc, strideC;
     const float* bias;
+    int bias_row;  // bias[row] instead of bias[col]
     int relu;
     int tiles_m, tiles_n;
     uint32_t* err;  // device error word
@@ -196,6 +197,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const bool vec = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                          ((p.strideC & 3) == 0);
         float* stg = reinterpret_cast<float*>(smem + RING_BYTES + 256) + (warp - 2) * (32 * STG_LD);
+        // a row bias is added in registers before epi(); epi() then sees no column bias
+        const float* cbias = p.bias_row ? nullptr : p.bias;
+        const float rbias = (p.bias_row && row < p.M) ? __ldg(p.bias + row) : 0.0f;
         if (ok) {
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
@@ -208,16 +212,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ptx::tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(rl[j]));
+                if (p.bias_row) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + rbias);
+                }
                 const float* abase = p.aux ? p.aux + (int64_t)bidx * p.stride_aux : nullptr;
                 if (vec && col0 + 32 <= p.N) {  // warp-uniform
                     // thread `lane` holds row q*32+lane: stage it ...
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
                         float4 v;
-                        v.x = epi(__uint_as_float(r[j + 0]), p.bias, col0 + j + 0, p.relu);
-                        v.y = epi(__uint_as_float(r[j + 1]), p.bias, col0 + j + 1, p.relu);
-                        v.z = epi(__uint_as_float(r[j + 2]), p.bias, col0 + j + 2, p.relu);
-                        v.w = epi(__uint_as_float(r[j + 3]), p.bias, col0 + j + 3, p.relu);
+                        v.x = epi(__uint_as_float(r[j + 0]), cbias, col0 + j + 0, p.relu);
+                        v.y = epi(__uint_as_float(r[j + 1]), cbias, col0 + j + 1, p.relu);
+                        v.z = epi(__uint_as_float(r[j + 2]), cbias, col0 + j + 2, p.relu);
+                        v.w = epi(__uint_as_float(r[j + 3]), cbias, col0 + j + 3, p.relu);
                         *reinterpret_cast<float4*>(stg + lane * STG_LD + j) = v;
                     }
                     __syncwarp();
@@ -246,7 +254,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         if (col0 + j >= p.N) continue;
-                        float v = epi(__uint_as_float(r[j]), p.bias, col0 + j, p.relu);
+                        float v = epi(__uint_as_float(r[j]), cbias, col0 + j, p.relu);
                         if (abase && !(__ldg(abase + (int64_t)row * p.ld_aux + col0 + j) > 0.0f)) v = 0.0f;
                         if (p.mc_store) ptx::multimem_st_f32(crow + col0 + j, v);
                         else crow[col0 + j] = v;
@@ -395,7 +403,7 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
 
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
-                   cudaStream_t s, int mc_store, const float* aux, int64_t ld_aux, int64_t stride_aux) {
+                   cudaStream_t s, int mc_store, const float* aux, int64_t ld_aux, int64_t stride_aux, int bias_row) {
     using namespace tc;
     const int Kp = (K + 3) & ~3;
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
@@ -415,7 +423,7 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
     Params p;
     p.M = M; p.N = N; p.K = K; p.batch = batch;
     p.C = C; p.ldc = ldc; p.strideC = strideC;
-    p.bias = bias; p.relu = relu;
+    p.bias = bias; p.bias_row = bias_row; p.relu = relu;
     p.tiles_m = (M + BM - 1) / BM;
     p.tiles_n = (N + BN - 1) / BN;
     p.err = err;
@@ -451,7 +459,7 @@ static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cud
     rc = tc_split(a.B, a.transB, a.ldb, a.strideB, a.N, a.K, a.batch, b_hi, b_lo, s);
     if (rc) return rc;
     return tc_gemm_planes(a_hi, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, a.C, a.ldc, a.strideC, a.bias, a.relu, err,
-                          s, 0, a.aux, a.ld_aux, a.stride_aux);
+                          s, 0, a.aux, a.ld_aux, a.stride_aux, a.bias_row);
 }
 
 int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {

@@ -44,9 +44,12 @@ def _operand(x, name: str):
     raise ValueError(f"{name}: unsupported strides {tuple(x.stride())} for shape {tuple(x.shape)}")
 
 
-def gemm(a, b, out=None, *, bias=None, relu: bool = False, mask=None, kernel: str = "auto", stream=None):
+def gemm(a, b, out=None, *, bias=None, row_bias=None, relu: bool = False, mask=None, kernel: str = "auto",
+         stream=None):
     """out = relu?(a @ b + bias) with a: [M,K] or [B,M,K], b: [K,N] or [B,K,N].
 
+    bias has N elements (one per column); row_bias, exclusive with it, has M
+    (one per row: a convolution's output channels).
     mask (a contiguous float32 tensor of out's shape) selects the ReLU-backward
     epilogue instead: out = (a @ b) * (mask > 0); it excludes bias and relu.
     Transposed views of either operand are consumed in place (NT / TN forms).
@@ -70,8 +73,13 @@ def gemm(a, b, out=None, *, bias=None, relu: bool = False, mask=None, kernel: st
     if bias is not None:
         if bias.dtype != torch.float32 or bias.numel() != N or not bias.is_contiguous():
             raise ValueError("bias must be a contiguous float32 tensor with N elements")
+    if row_bias is not None:
+        if bias is not None:
+            raise ValueError("bias and row_bias are exclusive")
+        if row_bias.dtype != torch.float32 or row_bias.numel() != M or not row_bias.is_contiguous():
+            raise ValueError("row_bias must be a contiguous float32 tensor with M elements")
     if mask is not None:
-        if bias is not None or relu:
+        if bias is not None or row_bias is not None or relu:
             raise ValueError("mask excludes bias and relu")
         if tuple(mask.shape) != shape or not mask.is_contiguous() or mask.dtype != torch.float32:
             raise ValueError(f"mask must be a contiguous float32 tensor of shape {shape}")
@@ -84,6 +92,9 @@ def gemm(a, b, out=None, *, bias=None, relu: bool = False, mask=None, kernel: st
     d.batch = batch
     d.bias = bias.data_ptr() if bias is not None else None
     d.epilogue = (_lib.EPI_BIAS if bias is not None else 0) | (_lib.EPI_RELU if relu else 0)
+    if row_bias is not None:
+        d.bias = row_bias.data_ptr()
+        d.epilogue = _lib.EPI_BIAS_ROW_RELU if relu else _lib.EPI_BIAS_ROW
     if mask is not None:
         d.epilogue = _lib.EPI_MASK
         d.aux, d.ld_aux, d.stride_aux = mask.data_ptr(), N, M * N

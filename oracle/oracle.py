@@ -8,6 +8,9 @@ product (jstorch_b200) never calls it.
   mlp_forward_backward                     fp64 restatement of one forward +
                                            backward of the reference's
                                            nn.Linear / ReLU / Sequential MLP
+  conv2d_f64 / conv_transpose2d_f64 /      fp64 restatements of the im2col-GEMM
+  conv2d_backward_weight_f64 /             convolution launchers (1-D = 2-D
+  conv_transpose2d_backward_weight_f64     with H = 1), tap by tap
 
 Reference citations are relative to the JsTorch project root.
 """
@@ -170,3 +173,137 @@ def mlp_forward_backward(x: np.ndarray, weights: list, biases: list) -> dict:
         if l > 0:
             g = dh[l] * (z[l - 1] > 0)
     return {"z": z, "h": h, "y": y, "dW": dW, "db": db, "dh": dh}
+
+
+# ------------------------------------------------------------- convolutions
+# Restated from native/ops/conv.cu with the tensor shapes of native/core/tensor.cpp:
+#   im2col            conv.cu:202-220   col[b, c*kk + kh*kW + kw, ho*Wo + wo] =
+#                                       x[b, c, ho*sH - pH + kh*dH, wo*sW - pW + kw*dW] (0 outside)
+#   conv2d            conv.cu:402-434   out[b, g] = W_g . col[b, g] (+ bias[co])
+#   conv_transpose2d  conv.cu:436-466   col[b, g] = W_g^T . x[b, g]; out = col2im(col) (+ bias)
+#   col2im            conv.cu:223-247   out[b, c, h, w] = sum of col entries whose tap maps to (h, w)
+#   backward weight   conv.cu:530-563   gw_g = sum_b go[b, g] . col[b, g]^T
+#                     conv.cu:600-627   gw_g = sum_b x[b, g] . im2col(go)[b, g]^T
+#   output sizes      tensor.cpp:469-470 (conv), 484-485 (transposed)
+# Each product is accumulated in fp64 tap by tap (no col matrix is formed).
+
+
+def conv_out_size(n, k, s, p, d):
+    """tensor.cpp:469: (n + 2p - d(k-1) - 1) / s + 1."""
+    return (n + 2 * p - d * (k - 1) - 1) // s + 1
+
+
+def conv_transpose_out_size(n, k, s, p, d, op=0):
+    """tensor.cpp:484: (n - 1)s - 2p + d(k-1) + op + 1."""
+    return (n - 1) * s - 2 * p + d * (k - 1) + op + 1
+
+
+def _pad_to(x, pH, pW, need_h, need_w):
+    """Zero-pad H by pH before and W by pW before, and after so that the
+    padded extents are at least need_h x need_w."""
+    H, W = x.shape[2], x.shape[3]
+    return np.pad(x, ((0, 0), (0, 0), (pH, max(0, need_h - H - pH)), (pW, max(0, need_w - W - pW))))
+
+
+def _taps(xp, kh, kw, dH, dW, sH, sW, Ho, Wo):
+    """xp[:, :, kh*dH + ho*sH, kw*dW + wo*sW] for ho < Ho, wo < Wo."""
+    return xp[:, :, kh * dH: kh * dH + sH * (Ho - 1) + 1: sH, kw * dW: kw * dW + sW * (Wo - 1) + 1: sW]
+
+
+def conv2d_f64(x, w, bias=None, stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1):
+    """Convolution (conv.cu:402-434): x [B, Ci, H, W], w [Co, Ci/g, kH, kW],
+    bias [Co] or None -> [B, Co, Ho, Wo] in fp64."""
+    x = np.asarray(x, np.float64)
+    w = np.asarray(w, np.float64)
+    B, Ci, H, W = x.shape
+    Co, Cig, kH, kW = w.shape
+    (sH, sW), (pH, pW), (dH, dW) = stride, padding, dilation
+    Ho, Wo = conv_out_size(H, kH, sH, pH, dH), conv_out_size(W, kW, sW, pW, dW)
+    Cog = Co // groups
+    xp = _pad_to(x, pH, pW, (Ho - 1) * sH + (kH - 1) * dH + 1, (Wo - 1) * sW + (kW - 1) * dW + 1)
+    out = np.zeros((B, Co, Ho, Wo))
+    for g in range(groups):
+        xg = xp[:, g * Cig:(g + 1) * Cig]
+        wg = w[g * Cog:(g + 1) * Cog]
+        for kh in range(kH):
+            for kw in range(kW):
+                out[:, g * Cog:(g + 1) * Cog] += np.einsum(
+                    "bchw,oc->bohw", _taps(xg, kh, kw, dH, dW, sH, sW, Ho, Wo), wg[:, :, kh, kw], optimize=True)
+    if bias is not None:
+        out += np.asarray(bias, np.float64)[None, :, None, None]
+    return out
+
+
+def conv_transpose2d_f64(x, w, bias=None, stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1,
+                         output_padding=(0, 0)):
+    """Transposed convolution (conv.cu:436-466): x [B, Ci, Hi, Wi],
+    w [Ci, Co/g, kH, kW] -> [B, Co, Ho, Wo] in fp64: input pixel (hi, wi)
+    scatters into output (hi*sH - pH + kh*dH, wi*sW - pW + kw*dW)."""
+    x = np.asarray(x, np.float64)
+    w = np.asarray(w, np.float64)
+    B, Ci, Hi, Wi = x.shape
+    _, Cog, kH, kW = w.shape
+    (sH, sW), (pH, pW), (dH, dW) = stride, padding, dilation
+    Co = Cog * groups
+    Cig = Ci // groups
+    Ho = conv_transpose_out_size(Hi, kH, sH, pH, dH, output_padding[0])
+    Wo = conv_transpose_out_size(Wi, kW, sW, pW, dW, output_padding[1])
+    Hc = max(Ho + pH, (Hi - 1) * sH + (kH - 1) * dH + 1)
+    Wc = max(Wo + pW, (Wi - 1) * sW + (kW - 1) * dW + 1)
+    canvas = np.zeros((B, Co, Hc, Wc))
+    for g in range(groups):
+        xg = x[:, g * Cig:(g + 1) * Cig]
+        wg = w[g * Cig:(g + 1) * Cig]
+        for kh in range(kH):
+            for kw in range(kW):
+                canvas[:, g * Cog:(g + 1) * Cog, kh * dH: kh * dH + sH * (Hi - 1) + 1: sH,
+                       kw * dW: kw * dW + sW * (Wi - 1) + 1: sW] += np.einsum("bchw,co->bohw", xg, wg[:, :, kh, kw], optimize=True)
+    out = canvas[:, :, pH:pH + Ho, pW:pW + Wo].copy()
+    if bias is not None:
+        out += np.asarray(bias, np.float64)[None, :, None, None]
+    return out
+
+
+def conv2d_backward_weight_f64(x, go, kernel, stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1):
+    """Weight gradient of conv2d (conv.cu:530-563): x [B, Ci, H, W],
+    go [B, Co, Ho, Wo] -> [Co, Ci/g, kH, kW] in fp64."""
+    x = np.asarray(x, np.float64)
+    go = np.asarray(go, np.float64)
+    B, Ci, H, W = x.shape
+    _, Co, Ho, Wo = go.shape
+    kH, kW = kernel
+    (sH, sW), (pH, pW), (dH, dW) = stride, padding, dilation
+    Cig, Cog = Ci // groups, Co // groups
+    xp = _pad_to(x, pH, pW, (Ho - 1) * sH + (kH - 1) * dH + 1, (Wo - 1) * sW + (kW - 1) * dW + 1)
+    gw = np.zeros((Co, Cig, kH, kW))
+    for g in range(groups):
+        xg = xp[:, g * Cig:(g + 1) * Cig]
+        gg = go[:, g * Cog:(g + 1) * Cog]
+        for kh in range(kH):
+            for kw in range(kW):
+                gw[g * Cog:(g + 1) * Cog, :, kh, kw] = np.einsum(
+                    "bohw,bchw->oc", gg, _taps(xg, kh, kw, dH, dW, sH, sW, Ho, Wo), optimize=True)
+    return gw
+
+
+def conv_transpose2d_backward_weight_f64(x, go, kernel, stride=(1, 1), padding=(0, 0), dilation=(1, 1), groups=1):
+    """Weight gradient of conv_transpose2d (conv.cu:600-627): x [B, Ci, Hi, Wi],
+    go [B, Co, Ho, Wo] -> [Ci, Co/g, kH, kW] in fp64; im2col of go over the
+    input grid: go[b, co, hi*sH - pH + kh*dH, wi*sW - pW + kw*dW] (0 outside)."""
+    x = np.asarray(x, np.float64)
+    go = np.asarray(go, np.float64)
+    B, Ci, Hi, Wi = x.shape
+    _, Co, Ho, Wo = go.shape
+    kH, kW = kernel
+    (sH, sW), (pH, pW), (dH, dW) = stride, padding, dilation
+    Cig, Cog = Ci // groups, Co // groups
+    gp = _pad_to(go, pH, pW, (Hi - 1) * sH + (kH - 1) * dH + 1, (Wi - 1) * sW + (kW - 1) * dW + 1)
+    gw = np.zeros((Ci, Cog, kH, kW))
+    for g in range(groups):
+        xg = x[:, g * Cig:(g + 1) * Cig]
+        gg = gp[:, g * Cog:(g + 1) * Cog]
+        for kh in range(kH):
+            for kw in range(kW):
+                gw[g * Cig:(g + 1) * Cig, :, kh, kw] = np.einsum(
+                    "bchw,bohw->co", xg, _taps(gg, kh, kw, dH, dW, sH, sW, Hi, Wi), optimize=True)
+    return gw

@@ -31,6 +31,34 @@ def test_every_header_function_is_exported():
         assert n in exported, n
 
 
+CONV_LAUNCHERS = ["launch_conv1d", "launch_conv_transpose1d", "launch_conv2d", "launch_conv_transpose2d",
+                  "launch_conv1d_backward_weight", "launch_conv2d_backward_weight",
+                  "launch_conv_transpose1d_backward_weight", "launch_conv_transpose2d_backward_weight"]
+
+
+def test_conv_header_matches_reference_names_and_is_exported():
+    names = _lib.header_functions(_lib.CONV_HEADER)
+    assert sorted(names) == sorted(CONV_LAUNCHERS)  # conv.cu:324-627, the eight im2col-GEMM sites
+    lib = _lib.load()
+    nm = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = {line.split()[-1] for line in nm.splitlines() if " T " in line}
+    for n in names:
+        assert hasattr(lib, n) and n in exported, n
+
+
+def test_conv_argument_validation_without_gpu():
+    """Bad geometry is rejected on the host before anything is launched."""
+    lib = _lib.load()
+    # groups that do not divide the channels
+    lib.launch_conv2d(16, 16, None, 16, 16, 1, 3, 8, 8, 4, 3, 3, 1, 1, 1, 1, 1, 1, 2, 8, 8, None)
+    assert lib.jst_get_last_status() == 1 and b"groups" in lib.jst_last_error()
+    # stride 0
+    lib.launch_conv1d(16, 16, None, 16, 16, 1, 4, 8, 4, 3, 0, 1, 1, 1, 8, None)
+    assert lib.jst_get_last_status() == 1
+    lib.launch_conv2d_backward_weight(16, 16, 16, 16, 1, 4, 8, 8, 4, 0, 3, 1, 1, 1, 1, 1, 1, 1, 8, 8, None)
+    assert lib.jst_get_last_status() == 1
+
+
 def test_desc_layout_matches_c():
     # jst_gemm_desc_init writes through the C struct; the ctypes mirror must
     # read back the same fields
@@ -44,7 +72,7 @@ def test_desc_layout_matches_c():
     assert d.batch == 1 and d.epilogue == 0 and d.kernel == 0 and d.stream is None
 
 
-@pytest.mark.parametrize("field,value", [("M", -1), ("batch", 0), ("transA", 2), ("epilogue", 9), ("kernel", 7),
+@pytest.mark.parametrize("field,value", [("M", -1), ("batch", 0), ("transA", 2), ("epilogue", 9), ("epilogue", 5), ("kernel", 7),
                                          ("lda", 2), ("ldc", 1)])
 def test_argument_validation_without_gpu(field, value):
     lib = _lib.load()

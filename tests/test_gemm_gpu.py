@@ -248,3 +248,22 @@ def test_ffma_split_k(jst, ta, tb, M, N, K, batch):
     np.testing.assert_array_equal(C1, c2.cpu().numpy().reshape(batch, M, N))
     for i in range(batch):
         _check(A[i], B[i], C1[i], bias=bias, relu=True)
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("relu", [False, True])
+@pytest.mark.parametrize("M,N,K,batch", [(300, 520, 96, 1), (64, 4096, 576, 3), (256, 1024, 1024, 1)])
+def test_row_bias_epilogue(jst, kernel, relu, M, N, K, batch):
+    """bias[i] per row (JST_EPI_BIAS_ROW*), the convolution bias layout, incl. split-K and batches."""
+    import torch
+    rng = np.random.default_rng(M + N + K + relu)
+    A = _rand(rng, batch, M, K)
+    B = _rand(rng, batch, K, N)
+    rb = _rand(rng, M)
+    a, b = (_dev(A), _dev(B)) if batch > 1 else (_dev(A[0]), _dev(B[0]))
+    c = jst.gemm(a, b, row_bias=_dev(rb), relu=relu, kernel=kernel)
+    plain = jst.gemm(a, b, kernel=kernel)
+    torch.cuda.synchronize()
+    C = c.cpu().numpy().reshape(batch, M, N)
+    P = plain.cpu().numpy().reshape(batch, M, N) + rb[None, :, None]
+    np.testing.assert_array_equal(C, np.maximum(P, 0) if relu else P)
