@@ -602,6 +602,50 @@ def run_config(args) -> None:
                     "value": gbs(t_up), "fromBuffer_gbs": gbs(t_up), "toArray_gbs": gbs(t_dn),
                     "pageable_sync_reference_style": {"h2d_gbs": gbs(r_up), "d2h_gbs": gbs(r_dn)},
                     "note": "wall clock per call incl. completion; pageable numpy source / destination"})
+    elif args.config == 7:
+        # conv2d through the im2col-GEMM launchers (conv.cu:402, :530): a 3x3, 256 -> 256
+        # channel layer on 56 x 56 images, batch 32
+        import torch.nn.functional as F
+
+        from jstorch_b200 import conv
+
+        B, Ci, Co, H, W = 32, 256, 256, 56, 56
+        gen = torch.Generator(device=dev).manual_seed(7)
+        x = torch.randn((B, Ci, H, W), device=dev, generator=gen)
+        w = torch.randn((Co, Ci, 3, 3), device=dev, generator=gen) / 48.0
+        bias = torch.randn(Co, device=dev, generator=gen)
+        go = torch.randn((B, Co, H, W), device=dev, generator=gen)
+        flops = 2.0 * B * Co * H * W * Ci * 9
+        _lib.profile_enable(True)
+        fwd = _time_device(lambda: conv.conv2d(x, w, bias, 1, 1), args.steps, args.warmup, stream)
+        ks_f = _lib.profile_read()
+        _lib.profile_enable(True)
+        bwd = _time_device(lambda: conv.conv2d_backward_weight(x, go, 3, 1, 1), args.steps, args.warmup, stream)
+        ks_b = _lib.profile_read()
+        _lib.profile_enable(False)
+        torch.backends.cudnn.allow_tf32 = False
+        cudnn = _time_device(lambda: F.conv2d(x, w, bias, 1, 1), args.steps, args.warmup, stream)
+
+        def ref_design():  # im2col + one TF32 GEMM per image + bias, as conv.cu:402-434
+            col = F.unfold(x, 3, padding=1)  # [B, Ci*9, H*W]
+            out = torch.empty((B, Co, H * W), device=dev)
+            for i in range(B):
+                torch.matmul(w.view(Co, -1), col[i], out=out[i])
+            return out + bias.view(1, Co, 1)
+
+        torch.backends.cuda.matmul.allow_tf32 = True
+        refd = _time_device(ref_design, args.steps, args.warmup, stream)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        tf = lambda ms: flops / (ms * 1e-3) / 1e12
+        per = lambda ks: {k: {"launches": v[0], "ms": v[1]} for k, v in ks.items()}
+        out.update({"metric": "conv2d 3x3 256->256, 56x56, batch 32: forward (launch_conv2d)", "unit": "TFLOP/s",
+                    "value": tf(fwd), "forward_ms": fwd, "backward_weight_ms": bwd,
+                    "backward_weight_tflops": tf(bwd), "kernels_forward": per(ks_f),
+                    "kernels_backward_weight": per(ks_b),
+                    "context": {"cudnn_fp32_ms": cudnn, "cudnn_fp32_tflops": tf(cudnn),
+                                "reference_design_tf32_ms": refd, "reference_design_tf32_tflops": tf(refd)},
+                    "note": "context rows: torch cuDNN conv2d with TF32 off; the reference's im2col + per-image "
+                            "GEMM loop restated with torch (TF32 on, as conv.cu:190-196)"})
     print(json.dumps(out), flush=True)
 
 
@@ -716,7 +760,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--size", type=int, default=SIZE, help="square GEMM size at N=1 (default 8192)")
-    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5, 6],
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5, 6, 7],
                     help="secondary measurement of one BASELINE configuration (0: the headline line)")
     ap.add_argument("--trace", action="store_true", help="N>1: add one traced step's timeline to the line")
     ap.add_argument("--c-gather", choices=["auto", "multicast", "copy", "nccl"], default="auto",

@@ -113,8 +113,11 @@ int jst_gemm_select_kernel(const jst_gemm_desc* d);
  * instead, and calls no cudaMalloc, cudaFree or other allocating routine.
  *   - Same descriptor and result as jst_gemm_ex with kernel = TC3XTF32
  *     (`kernel` must be AUTO or TC3XTF32).  The caller passes A, B, C, bias.
- *   - Limit: 2 * Kp * (M + N) * batch * 4 bytes <= 64 MiB, Kp = K rounded up
- *     to a multiple of 4 (e.g. 2048^3 fits); larger requests return
+ *   - Limit: the tensor-core path's scratch must fit 64 MiB: hi/lo planes of
+ *     2 * Kp * (M * Ba + N * Bb) * 4 bytes (Kp = K rounded up to a multiple
+ *     of 4; Ba, Bb = batch, or 1 for an operand with batch stride 0), plus
+ *     S * batch * M * N * 4 bytes of split-K partials when the output tiles
+ *     fill less than half the SMs (e.g. 2048^3 fits); larger requests return
  *     JST_ERR_ARG without launching.
  *   - The array exists once per device, for the life of the process, and is
  *     shared by all calls: calls whose work overlaps on the GPU (different

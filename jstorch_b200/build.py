@@ -34,7 +34,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
            "--expt-relaxed-constexpr", "-DNDEBUG", f"-I{INCLUDE}"] + ARCH
 
-GEMM_SOURCES = ["gemm_api.cu", "gemm_ffma.cu", "gemm_tc.cu", "conv.cu", "profile.cu"]
+GEMM_SOURCES = ["gemm_api.cu", "gemm_ffma.cu", "gemm_tc.cu", "splitk.cu", "conv.cu", "profile.cu"]
 GEMM_HEADERS = ["gemm_internal.h", "ptx.cuh"]
 GEMM_LIB = PKG / "libjstorch_gemm.so"
 

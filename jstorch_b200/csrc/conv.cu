@@ -38,52 +38,54 @@ struct Geo {
 
 // col (batch-outer) [b][c*kH*kW + kh*kW + kw][ho*Wo + wo]  -- conv.cu:202-220
 // col (batch-inner) [c*kH*kW + kh*kW + kw][b][ho*Wo + wo]
+// One block per row of the column matrix (fixed b, c, kh, kw): the row's
+// coordinates are decoded once, the threads walk its Ho*Wo entries, so the
+// stores are coalesced and (stride 1) so are the loads.
 template <bool INNER>
 __global__ void im2col_kernel(const float* __restrict__ in, float* __restrict__ col, const Geo g) {
-    const int64_t N = (int64_t)g.Ho * g.Wo;
-    const int64_t kk = (int64_t)g.kH * g.kW;
-    const int64_t total = (int64_t)g.B * g.C * kk * N;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        // i enumerates the destination in memory order
-        int64_t b, r, n;
-        if (INNER) {
-            n = i % N;
-            const int64_t t = i / N;
-            b = t % g.B;
-            r = t / g.B;
-        } else {
-            n = i % N;
-            const int64_t t = i / N;
-            r = t % (g.C * kk);
-            b = t / (g.C * kk);
-        }
-        const int c = (int)(r / kk);
-        const int tap = (int)(r % kk);
-        const int kh = tap / g.kW, kw = tap % g.kW;
-        const int ho = (int)(n / g.Wo), wo = (int)(n % g.Wo);
-        const int hi = ho * g.sH - g.pH + kh * g.dH;
-        const int wi = wo * g.sW - g.pW + kw * g.dW;
+    const int N = g.Ho * g.Wo;
+    const int kk = g.kH * g.kW;
+    const int64_t row = blockIdx.x + (int64_t)blockIdx.y * gridDim.x;  // destination row
+    int b, r;
+    if (INNER) {
+        b = (int)(row % g.B);
+        r = (int)(row / g.B);
+    } else {
+        r = (int)(row % ((int64_t)g.C * kk));
+        b = (int)(row / ((int64_t)g.C * kk));
+    }
+    if (b >= g.B) return;
+    const int c = r / kk, tap = r % kk;
+    const int oh = (tap / g.kW) * g.dH - g.pH, ow = (tap % g.kW) * g.dW - g.pW;
+    const float* src = in + ((int64_t)b * g.C + c) * g.H * g.W;
+    float* dst = col + row * N;
+    for (int n = threadIdx.x; n < N; n += blockDim.x) {
+        const int ho = n / g.Wo, wo = n - ho * g.Wo;
+        const int hi = ho * g.sH + oh, wi = wo * g.sW + ow;
         float v = 0.0f;
-        if (hi >= 0 && hi < g.H && wi >= 0 && wi < g.W) v = __ldg(in + (((b * g.C + c) * (int64_t)g.H + hi) * g.W + wi));
-        col[i] = v;
+        if ((unsigned)hi < (unsigned)g.H && (unsigned)wi < (unsigned)g.W) v = __ldg(src + hi * g.W + wi);
+        dst[n] = v;
     }
 }
 
 // output[b][c][h][w] = sum over taps of col[b][c*kk + tap][hi*Wi + wi] (+ bias[c])
 // -- conv.cu:223-247, the bias (conv.cu:250-257) added after the tap sum.
 // Here g.H x g.W is the output image and g.Ho x g.Wo the column spatial size.
+// One block per output plane (b, c).
 __global__ void col2im_kernel(const float* __restrict__ col, float* __restrict__ out, const float* __restrict__ bias,
                               const Geo g) {
-    const int64_t total = (int64_t)g.B * g.C * g.H * g.W;
-    const int64_t Ni = (int64_t)g.Ho * g.Wo;
+    const int64_t bc = blockIdx.x + (int64_t)blockIdx.y * gridDim.x;
+    if (bc >= (int64_t)g.B * g.C) return;
+    const int c = (int)(bc % g.C);
+    const int HW = g.H * g.W;
+    const int Ni = g.Ho * g.Wo;
     const int kk = g.kH * g.kW;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int w = (int)(i % g.W);
-        const int h = (int)((i / g.W) % g.H);
-        const int64_t bc = i / ((int64_t)g.H * g.W);
-        const int c = (int)(bc % g.C);
+    const float* cb = col + bc * kk * Ni;
+    const float bv = bias ? __ldg(bias + c) : 0.0f;
+    float* o = out + bc * HW;
+    for (int i = threadIdx.x; i < HW; i += blockDim.x) {
+        const int h = i / g.W, w = i - h * g.W;
         float sum = 0.0f;
-        const float* cb = col + bc * kk * Ni;
         for (int kh = 0; kh < g.kH; ++kh) {
             const int nh = h + g.pH - kh * g.dH;
             if (nh < 0 || nh % g.sH) continue;
@@ -94,55 +96,57 @@ __global__ void col2im_kernel(const float* __restrict__ col, float* __restrict__
                 if (nw < 0 || nw % g.sW) continue;
                 const int wi = nw / g.sW;
                 if (wi >= g.Wo) continue;
-                sum += __ldg(cb + (int64_t)(kh * g.kW + kw) * Ni + (int64_t)hi * g.Wo + wi);
+                sum += __ldg(cb + (int64_t)(kh * g.kW + kw) * Ni + hi * g.Wo + wi);
             }
         }
-        if (bias) sum += __ldg(bias + c);
-        out[i] = sum;
+        if (bias) sum += bv;
+        o[i] = sum;
     }
 }
 
-// dst[c][b][n] = src[b][c][n]
-__global__ void permute_bcn_kernel(const float* __restrict__ src, float* __restrict__ dst, int B, int C, int64_t N) {
-    const int64_t total = (int64_t)B * C * N;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t n = i % N;
-        const int64_t t = i / N;
-        const int b = (int)(t % B);
-        const int c = (int)(t / B);
-        dst[i] = __ldg(src + ((int64_t)b * C + c) * N + n);
-    }
+// dst[c][b][n] = src[b][c][n], one block per (c, b) row
+__global__ void permute_bcn_kernel(const float* __restrict__ src, float* __restrict__ dst, int B, int C, int N) {
+    const int64_t row = blockIdx.x + (int64_t)blockIdx.y * gridDim.x;  // c * B + b
+    if (row >= (int64_t)B * C) return;
+    const int b = (int)(row % B), c = (int)(row / B);
+    const float* s = src + ((int64_t)b * C + c) * N;
+    float* d = dst + row * N;
+    for (int n = threadIdx.x; n < N; n += blockDim.x) d[n] = __ldg(s + n);
 }
 
-int grid_for(int64_t n) { return (int)std::min<int64_t>((n + 255) / 256, 148LL * 16); }
+// Grid of `rows` blocks as (x, y) with x <= 65535 * 1024.
+dim3 row_grid(int64_t rows) {
+    const int64_t x = std::min<int64_t>(rows, 1 << 20);
+    return dim3((unsigned)x, (unsigned)((rows + x - 1) / x));
+}
 
 int im2col(const float* in, float* col, const Geo& g, bool inner, cudaStream_t s) {
-    const int64_t total = (int64_t)g.B * g.C * g.kH * g.kW * g.Ho * g.Wo;
-    if (total == 0) return JST_OK;
+    const int64_t rows = (int64_t)g.B * g.C * g.kH * g.kW;
+    if (rows == 0 || (int64_t)g.Ho * g.Wo == 0) return JST_OK;
     {
         ProfScope prof(s, KID_CONV);
-        if (inner) im2col_kernel<true><<<grid_for(total), 256, 0, s>>>(in, col, g);
-        else im2col_kernel<false><<<grid_for(total), 256, 0, s>>>(in, col, g);
+        if (inner) im2col_kernel<true><<<row_grid(rows), 256, 0, s>>>(in, col, g);
+        else im2col_kernel<false><<<row_grid(rows), 256, 0, s>>>(in, col, g);
     }
     return cudaPeekAtLastError() == cudaSuccess ? JST_OK : set_status(JST_ERR_CUDA, "im2col launch failed");
 }
 
 int col2im(const float* col, float* out, const float* bias, const Geo& g, cudaStream_t s) {
-    const int64_t total = (int64_t)g.B * g.C * g.H * g.W;
-    if (total == 0) return JST_OK;
+    const int64_t planes = (int64_t)g.B * g.C;
+    if (planes == 0 || (int64_t)g.H * g.W == 0) return JST_OK;
     {
         ProfScope prof(s, KID_CONV);
-        col2im_kernel<<<grid_for(total), 256, 0, s>>>(col, out, bias, g);
+        col2im_kernel<<<row_grid(planes), 256, 0, s>>>(col, out, bias, g);
     }
     return cudaPeekAtLastError() == cudaSuccess ? JST_OK : set_status(JST_ERR_CUDA, "col2im launch failed");
 }
 
 int permute_bcn(const float* src, float* dst, int B, int C, int64_t N, cudaStream_t s) {
-    const int64_t total = (int64_t)B * C * N;
-    if (total == 0) return JST_OK;
+    const int64_t rows = (int64_t)B * C;
+    if (rows == 0 || N == 0) return JST_OK;
     {
         ProfScope prof(s, KID_CONV);
-        permute_bcn_kernel<<<grid_for(total), 256, 0, s>>>(src, dst, B, C, N);
+        permute_bcn_kernel<<<row_grid(rows), 256, 0, s>>>(src, dst, B, C, (int)N);
     }
     return cudaPeekAtLastError() == cudaSuccess ? JST_OK : set_status(JST_ERR_CUDA, "permute launch failed");
 }

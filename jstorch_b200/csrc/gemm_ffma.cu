@@ -16,8 +16,9 @@
 //
 // Split K: when the tiles of C cannot fill the SMs (the M = 256 layers of an
 // MLP, 512^3), K is cut into S slices of whole BK steps; CTA (tile, slice)
-// writes its partial tile to a stream-ordered workspace and a second kernel
-// adds the S partials in slice order (deterministic) and applies the epilogue.
+// writes its partial tile to a stream-ordered workspace and the split-K
+// reduce (splitk.cu) adds the S partials in slice order and applies the
+// epilogue.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -254,54 +255,6 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
     }
 }
 
-// C = epilogue(sum over s of part[s]), the slices added in order.  One thread
-// per W consecutive columns of a row: W = 4 (float4 loads) when N % 4 == 0,
-// else W = 1.
-template <int W>
-__global__ void splitk_reduce_kernel(const Params p, int batch) {
-    const int nw = p.N / W;
-    const int64_t total = (int64_t)batch * p.M * nw;
-    const int64_t plane = (int64_t)batch * p.M * p.N;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int cw = (int)(i % nw);
-        const int64_t br = i / nw;
-        const int row = (int)(br % p.M);
-        const int b = (int)(br / p.M);
-        const int col = cw * W;
-        const int64_t off = ((int64_t)b * p.M + row) * p.N + col;
-        float v[W];
-#pragma unroll
-        for (int j = 0; j < W; ++j) v[j] = 0.0f;
-        for (int sl = 0; sl < p.kslices; ++sl) {
-            const float* src = p.part + sl * plane + off;
-            if constexpr (W == 4) {
-                const float4 x = __ldg(reinterpret_cast<const float4*>(src));
-                v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w;
-            } else {
-                v[0] += __ldg(src);
-            }
-        }
-        float* crow = p.C + (int64_t)b * p.strideC + (int64_t)row * p.ldc;
-        const float* arow = p.aux ? p.aux + (int64_t)b * p.stride_aux + (int64_t)row * p.ld_aux : nullptr;
-#pragma unroll
-        for (int j = 0; j < W; ++j) {
-            float x = v[j];
-            if (p.bias) x += __ldg(p.bias + (p.bias_row ? row : col + j));
-            if (p.relu) x = fmaxf(x, 0.0f);
-            if (arow && !(__ldg(arow + col + j) > 0.0f)) x = 0.0f;
-            v[j] = x;
-        }
-        if constexpr (W == 4) {
-            if (p.vecC) {
-                *reinterpret_cast<float4*>(crow + col) = make_float4(v[0], v[1], v[2], v[3]);
-                continue;
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < W; ++j) crow[col + j] = v[j];
-    }
-}
-
 template <int BM, int BN, int BK, int RM, int RN>
 static void launch_cfg(const Params& p, int batch, bool TA, bool TB, cudaStream_t s) {
     constexpr int threads = (BM / (4 * RM)) * (BN / (4 * RN));
@@ -356,17 +309,9 @@ int ffma_gemm_run(const GemmArgs& a, cudaStream_t s) {
         return set_status(JST_ERR_CUDA, "ffma_gemm_kernel launch failed");
     }
     if (p.kslices > 1) {
-        const bool w4 = (a.N & 3) == 0;
-        const int64_t total = (int64_t)a.batch * a.M * (w4 ? a.N / 4 : a.N);
-        const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
-        {
-            ProfScope prof(s, KID_FFMA_GEMM);
-            if (w4) splitk_reduce_kernel<4><<<blocks, 256, 0, s>>>(p, a.batch);
-            else splitk_reduce_kernel<1><<<blocks, 256, 0, s>>>(p, a.batch);
-        }
-        const cudaError_t le = cudaPeekAtLastError();
+        const int rc = splitk_reduce_run(splitk_reduce_args(a, p.part, p.kslices), s);
         const int frc = workspace_free(ws, s);
-        if (le != cudaSuccess) return set_status(JST_ERR_CUDA, "split-K reduce launch failed");
+        if (rc) return rc;
         if (frc) return frc;
     }
     return JST_OK;

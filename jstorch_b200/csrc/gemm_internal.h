@@ -46,12 +46,18 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
 // Tensor-core kernel alone on existing planes (A planes M rows, B planes N rows).
 // mc_store: C is the multicast view of a multicast-backed buffer; every tile
 // is stored once through it and reaches every GPU of the team.
+// a_bcast / b_bcast: that operand's planes hold one batch entry shared by all.
+// kslices > 1: split K into that many slices; C then receives the raw partial
+// products part[slice][batch][M][N] (ldc = N, strideC = M * N, no epilogue) for
+// splitk_reduce_run to combine.
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
                    cudaStream_t s, int mc_store = 0, const float* aux = nullptr, int64_t ld_aux = 0,
-                   int64_t stride_aux = 0, int bias_row = 0);
+                   int64_t stride_aux = 0, int bias_row = 0, int a_bcast = 0, int b_bcast = 0, int kslices = 1);
+// split-K slices the tensor-core path uses for `a` (1: none)
+int tc_split_k(const GemmArgs& a);
 
-// FFMA SIMT path (no workspace)
+// FFMA SIMT path
 int ffma_gemm_run(const GemmArgs& a, cudaStream_t s);
 // split-K plan of the FFMA kernel (slices = 1: none) and its workspace size
 struct SplitK {
@@ -63,6 +69,21 @@ size_t ffma_workspace_bytes(const GemmArgs& a);
 // K == 0: C = epilogue(0)
 int fill_epilogue_run(const GemmArgs& a, cudaStream_t s);
 
+// Reduce of a split-K GEMM (splitk.cu): C = epilogue(sum over slices of part).
+struct SplitKReduce {
+    const float* part;  // [slices][batch][M][N] packed
+    int slices, batch, M, N;
+    float* C;
+    int64_t ldc, strideC;
+    const float* bias;
+    int bias_row, relu;
+    const float* aux;
+    int64_t ld_aux, stride_aux;
+    int vecC;
+};
+SplitKReduce splitk_reduce_args(const GemmArgs& a, const float* part, int slices);
+int splitk_reduce_run(const SplitKReduce& r, cudaStream_t s);
+
 // ---- launch accounting / optional event timing (profile.cu)
 enum KernelId {
     KID_TC_GEMM = 0,
@@ -71,6 +92,7 @@ enum KernelId {
     KID_FFMA_GEMM,
     KID_FILL,
     KID_CONV,  // im2col / col2im / permute of the convolution launchers
+    KID_SPLITK_REDUCE,
     KERNEL_ID_COUNT
 };
 

@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -79,6 +80,9 @@ struct Params {
     int mc_store;   // C is a multicast address: store with multimem.st (fused all-gather)
     const float* aux;  // mask epilogue: C *= (aux > 0)
     int64_t ld_aux, stride_aux;
+    int a_bcast, b_bcast;  // operand planes hold one batch entry shared by every batch
+    int kslices;           // > 1: split K; C receives partials [slice][batch][M][N]
+    int kb_per_slice;      // BK steps per slice
 };
 
 __device__ __forceinline__ float epi(float v, const float* bias, int col, int relu) {
@@ -105,9 +109,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     // grouped rasterisation: 8 tile-rows share a band so concurrently running
     // CTAs reuse the same B panels from L2
+    // CTA index = ((bidx * kslices) + slice) * tiles + tile: the CTAs of one
+    // K slice run next to each other and share its operand panels in L2
     const int tiles_per_batch = p.tiles_m * p.tiles_n;
-    const int bidx = blockIdx.x / tiles_per_batch;
     const int t = blockIdx.x % tiles_per_batch;
+    const int zs = blockIdx.x / tiles_per_batch;
+    const int slice = zs % p.kslices;
+    const int bidx = zs / p.kslices;
     constexpr int GROUP = 8;
     const int group_span = GROUP * p.tiles_n;
     const int g = t / group_span;
@@ -117,7 +125,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int tn = (t % group_span) / gm;
     const int m0 = tm * BM;
     const int n0 = tn * BN;
-    const int num_kb = (p.K + BK - 1) / BK;
+    const int kb0 = slice * p.kb_per_slice;  // this CTA's K steps: [kb0, kb0 + num_kb)
+    const int num_kb = min((p.K + BK - 1) / BK - kb0, p.kb_per_slice);
+    const int za = p.a_bcast ? 0 : bidx, zb = p.b_bcast ? 0 : bidx;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -147,11 +157,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!ptx::mbar_wait(&empty_bar[s], phase ^ 1, err)) break;
                 uint8_t* st = smem + s * STAGE_BYTES;
                 ptx::mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
-                const int kx = kb * BK;
-                ptx::tma_load_3d(st, &tm_a_hi, &full_bar[s], kx, m0, bidx);
-                ptx::tma_load_3d(st + A_TILE_BYTES, &tm_a_lo, &full_bar[s], kx, m0, bidx);
-                ptx::tma_load_3d(st + 2 * A_TILE_BYTES, &tm_b_hi, &full_bar[s], kx, n0, bidx);
-                ptx::tma_load_3d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_b_lo, &full_bar[s], kx, n0, bidx);
+                const int kx = (kb0 + kb) * BK;
+                ptx::tma_load_3d(st, &tm_a_hi, &full_bar[s], kx, m0, za);
+                ptx::tma_load_3d(st + A_TILE_BYTES, &tm_a_lo, &full_bar[s], kx, m0, za);
+                ptx::tma_load_3d(st + 2 * A_TILE_BYTES, &tm_b_hi, &full_bar[s], kx, n0, zb);
+                ptx::tma_load_3d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_b_lo, &full_bar[s], kx, n0, zb);
             }
         }
     } else if (warp == 1) {
@@ -192,7 +202,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
         const int row = m0 + q * 32 + lane;
         const bool row_ok = ok && row < p.M;
-        float* cbase = p.C + (int64_t)bidx * p.strideC;
+        float* cbase = p.C + (int64_t)(p.kslices > 1 ? slice * p.batch + bidx : bidx) * p.strideC;
         float* crow = cbase + (int64_t)row * p.ldc;
         const bool vec = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                          ((p.strideC & 3) == 0);
@@ -390,9 +400,31 @@ static int launch_split(const float* src, bool kmajor, int64_t ld, int64_t sstri
 
 }  // namespace tc
 
+// Split K when the output tiles fill less than one wave of 148 CTAs (one CTA
+// per SM): as many slices as still fit in the wave, each at least 64 BK steps
+// (K = 1024) long, at most 16.  The count is normalised so that no slice is
+// empty.
+int tc_split_k(const GemmArgs& a) {
+    const int64_t tiles = (int64_t)((a.M + tc::BM - 1) / tc::BM) * ((a.N + tc::BN - 1) / tc::BN) * a.batch;
+    const int num_kb = (a.K + tc::BK - 1) / tc::BK;
+    if (tiles <= 0 || tiles >= 148 / 2) return 1;
+    int S = (int)std::min<int64_t>(std::min<int64_t>(148 / tiles, num_kb / 64), 16);
+    if (S <= 1) return 1;
+    const int per = (num_kb + S - 1) / S;
+    return (num_kb + per - 1) / per;
+}
+
+// Planes of the operands that vary over the batch; a broadcast (stride 0)
+// operand is split once.  Then the split-K partials, if any.
+static bool a_broadcast(const GemmArgs& a) { return a.batch > 1 && a.strideA == 0; }
+static bool b_broadcast(const GemmArgs& a) { return a.batch > 1 && a.strideB == 0; }
+
 size_t tc_workspace_bytes(const GemmArgs& a) {
     const size_t Kp = (size_t)((a.K + 3) & ~3);
-    return 2 * Kp * ((size_t)a.M + (size_t)a.N) * (size_t)a.batch * sizeof(float);
+    const size_t ab = a_broadcast(a) ? 1 : (size_t)a.batch, bb = b_broadcast(a) ? 1 : (size_t)a.batch;
+    const int S = tc_split_k(a);
+    const size_t part = S > 1 ? (size_t)S * a.batch * a.M * a.N : 0;
+    return (2 * Kp * ((size_t)a.M * ab + (size_t)a.N * bb) + part) * sizeof(float);
 }
 
 int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows, int K, int batch, float* hi,
@@ -403,12 +435,19 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
 
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
-                   cudaStream_t s, int mc_store, const float* aux, int64_t ld_aux, int64_t stride_aux, int bias_row) {
+                   cudaStream_t s, int mc_store, const float* aux, int64_t ld_aux, int64_t stride_aux, int bias_row,
+                   int a_bcast, int b_bcast, int kslices) {
     using namespace tc;
     const int Kp = (K + 3) & ~3;
+    const int num_kb = (K + BK - 1) / BK;
+    if (kslices < 1 || kslices > num_kb) return set_status(JST_ERR_ARG, "tc: bad split-K slice count");
+    const int kb_per_slice = (num_kb + kslices - 1) / kslices;
+    if ((num_kb + kb_per_slice - 1) / kb_per_slice != kslices)  // a slice would be empty
+        return set_status(JST_ERR_ARG, "tc: split-K slice count leaves a slice empty");
+    const int ab = a_bcast ? 1 : batch, bb = b_bcast ? 1 : batch;
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-    if (!make_plane_map(&m_ahi, a_hi, K, M, batch, Kp, BM) || !make_plane_map(&m_alo, a_lo, K, M, batch, Kp, BM) ||
-        !make_plane_map(&m_bhi, b_hi, K, N, batch, Kp, BN) || !make_plane_map(&m_blo, b_lo, K, N, batch, Kp, BN))
+    if (!make_plane_map(&m_ahi, a_hi, K, M, ab, Kp, BM) || !make_plane_map(&m_alo, a_lo, K, M, ab, Kp, BM) ||
+        !make_plane_map(&m_bhi, b_hi, K, N, bb, Kp, BN) || !make_plane_map(&m_blo, b_lo, K, N, bb, Kp, BN))
         return set_status(JST_ERR_CUDA, "cuTensorMapEncodeTiled failed");
 
     static bool attr_set[64] = {};
@@ -431,7 +470,11 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
     p.aux = aux;
     p.ld_aux = ld_aux;
     p.stride_aux = stride_aux;
-    const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * batch;
+    p.a_bcast = a_bcast;
+    p.b_bcast = b_bcast;
+    p.kslices = kslices;
+    p.kb_per_slice = kb_per_slice;
+    const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * batch * kslices;
     if (grid > 0x7fffffff) return set_status(JST_ERR_ARG, "tc: too many tiles");
     {
         ProfScope prof(s, KID_TC_GEMM);
@@ -446,20 +489,29 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
 static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cudaStream_t s) {
     const int Kp = (a.K + 3) & ~3;
     float* ws = static_cast<float*>(workspace);
-    const size_t a_plane = (size_t)a.batch * a.M * Kp;
-    const size_t b_plane = (size_t)a.batch * a.N * Kp;
+    const bool abc = a_broadcast(a), bbc = b_broadcast(a);
+    const int ab = abc ? 1 : a.batch, bb = bbc ? 1 : a.batch;
+    const size_t a_plane = (size_t)ab * a.M * Kp;
+    const size_t b_plane = (size_t)bb * a.N * Kp;
     float* a_hi = ws;
     float* a_lo = a_hi + a_plane;
     float* b_hi = a_lo + a_plane;
     float* b_lo = b_hi + b_plane;
+    float* part = b_lo + b_plane;
     // op(A) rows are M: K-major unless A is stored transposed.
-    int rc = tc_split(a.A, !a.transA, a.lda, a.strideA, a.M, a.K, a.batch, a_hi, a_lo, s);
+    int rc = tc_split(a.A, !a.transA, a.lda, a.strideA, a.M, a.K, ab, a_hi, a_lo, s);
     if (rc) return rc;
     // op(B)^T rows are N: K-major when B is stored [N, K] (transB).
-    rc = tc_split(a.B, a.transB, a.ldb, a.strideB, a.N, a.K, a.batch, b_hi, b_lo, s);
+    rc = tc_split(a.B, a.transB, a.ldb, a.strideB, a.N, a.K, bb, b_hi, b_lo, s);
     if (rc) return rc;
-    return tc_gemm_planes(a_hi, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, a.C, a.ldc, a.strideC, a.bias, a.relu, err,
-                          s, 0, a.aux, a.ld_aux, a.stride_aux, a.bias_row);
+    const int S = tc_split_k(a);
+    if (S <= 1)
+        return tc_gemm_planes(a_hi, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, a.C, a.ldc, a.strideC, a.bias, a.relu,
+                              err, s, 0, a.aux, a.ld_aux, a.stride_aux, a.bias_row, abc, bbc, 1);
+    rc = tc_gemm_planes(a_hi, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, part, a.N, (int64_t)a.M * a.N, nullptr, 0, err,
+                        s, 0, nullptr, 0, 0, 0, abc, bbc, S);
+    if (rc) return rc;
+    return splitk_reduce_run(splitk_reduce_args(a, part, S), s);
 }
 
 int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {

@@ -267,3 +267,67 @@ def test_row_bias_epilogue(jst, kernel, relu, M, N, K, batch):
     C = c.cpu().numpy().reshape(batch, M, N)
     P = plain.cpu().numpy().reshape(batch, M, N) + rb[None, :, None]
     np.testing.assert_array_equal(C, np.maximum(P, 0) if relu else P)
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False)])
+@pytest.mark.parametrize("M,N,K,batch", [(256, 2304, 8192, 1), (128, 300, 20000, 1), (200, 256, 4100, 2)])
+def test_tc_split_k(jst, ta, tb, M, N, K, batch):
+    """Tensor-core GEMMs with few output tiles and a long K run split into
+    K slices plus the fixed-order reduce: bias + ReLU epilogue, oracle bound,
+    bit-identical reruns."""
+    import torch
+    rng = np.random.default_rng(M + N + K + batch + 2 * ta + tb)
+    A = _rand(rng, batch, M, K)
+    B = _rand(rng, batch, K, N)
+    bias = _rand(rng, N)
+    a = _dev(np.ascontiguousarray(A.transpose(0, 2, 1))).transpose(1, 2) if ta else _dev(A)
+    b = _dev(np.ascontiguousarray(B.transpose(0, 2, 1))).transpose(1, 2) if tb else _dev(B)
+    if batch == 1:
+        a, b = a[0], b[0]
+    c1 = jst.gemm(a, b, bias=_dev(bias), relu=True, kernel="tc3xtf32")
+    c2 = jst.gemm(a, b, bias=_dev(bias), relu=True, kernel="tc3xtf32")
+    torch.cuda.synchronize()
+    C1 = c1.cpu().numpy().reshape(batch, M, N)
+    np.testing.assert_array_equal(C1, c2.cpu().numpy().reshape(batch, M, N))
+    rows = np.arange(0, M, 7)
+    for i in range(batch):
+        _check(A[i], B[i], C1[i], bias=bias, relu=True, rows=rows)
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_broadcast_operand(jst, kernel):
+    """A batch stride of 0 (one operand shared by the whole batch, as the
+    convolution weights) through jst_gemm_ex."""
+    import torch
+    rng = np.random.default_rng(17)
+    M, N, K, batch = 256, 1024, 576, 6
+    W = _rand(rng, M, K)
+    X = _rand(rng, batch, K, N)
+    w, x = _dev(W), _dev(X)
+    c = torch.empty((batch, M, N), device="cuda")
+    d = _lib_desc(w, x, c, M, N, K, batch, strideA=0, strideB=K * N, kernel=kernel)
+    jst._lib.check(jst._lib.load().jst_gemm_ex(ctypes.byref(d)))
+    torch.cuda.synchronize()
+    C = c.cpu().numpy()
+    for i in range(batch):
+        _check(W, X[i], C[i])
+    W2 = _rand(rng, batch, K, M)  # B broadcast, A transposed per batch
+    d = _lib_desc(_dev(W2), _dev(X[0]), c, M, N, K, batch, strideA=K * M, strideB=0, transA=1, lda=M, kernel=kernel)
+    jst._lib.check(jst._lib.load().jst_gemm_ex(ctypes.byref(d)))
+    torch.cuda.synchronize()
+    C = c.cpu().numpy()
+    for i in range(batch):
+        _check(W2[i], X[0], C[i], ta=True)
+
+
+def _lib_desc(a, b, c, M, N, K, batch, *, strideA, strideB, transA=0, lda=None, kernel="auto"):
+    from jstorch_b200 import _lib
+    d = _lib.GemmDesc()
+    _lib.load().jst_gemm_desc_init(ctypes.byref(d), M, N, K, a.data_ptr(), b.data_ptr(), c.data_ptr())
+    d.batch = batch
+    d.transA = transA
+    if lda is not None:
+        d.lda = lda
+    d.strideA, d.strideB, d.strideC = strideA, strideB, M * N
+    d.kernel = _lib.KERNELS[kernel]
+    return d
