@@ -15,6 +15,10 @@
 //     loop of one NT GEMM (K = B * N), batched over the groups;
 //   * a 1 x 1, stride-1, unpadded conv2d uses the input as its column matrix
 //     (no im2col pass);
+//   * when the GEMM runs on the tensor-core kernel, im2col is fused into its
+//     split pass: the hi / lo tf32 planes the kernel streams are written
+//     straight from the image, and the column matrix never exists in memory
+//     (col_buf is left untouched);
 //   * indices are 64-bit; 1-D launchers are the 2-D ones with H = 1.
 // All GEMMs run in fp32 with the library's kernel choice (3xTF32 tensor-core
 // or FFMA), so the results meet the path's error bound, unlike the TF32
@@ -26,6 +30,7 @@
 
 #include "../../include/jstorch_conv.h"
 #include "gemm_internal.h"
+#include "ptx.cuh"
 
 namespace jst {
 namespace conv {
@@ -114,6 +119,117 @@ __global__ void permute_bcn_kernel(const float* __restrict__ src, float* __restr
     for (int n = threadIdx.x; n < N; n += blockDim.x) d[n] = __ldg(s + n);
 }
 
+// ---- im2col fused with the 3xTF32 split (hi = rn_tf32(v), lo = rn_tf32(v - hi))
+
+// Forward operand: planes [b][n][Kp] of the column matrix of one group,
+// element (k = c*kk + tap, n) read from image channel c0 + c.  A 32 x 32 tile
+// goes through shared memory so that the image reads (along n) and the plane
+// writes (along k) are both coalesced.  A block covers 32 pixels and
+// KT_PER_BLOCK tiles of k; the (channel, tap) offsets of its k values are
+// decoded once into shared memory, so the element loop has no division.
+constexpr int KT_PER_BLOCK = 4;
+__global__ void __launch_bounds__(256) im2col_split_t_kernel(const float* __restrict__ x, const Geo g, int c0, int Kg,
+                                                             int Kp, float* __restrict__ hi, float* __restrict__ lo) {
+    __shared__ float tile[32][33];
+    __shared__ int64_t k_base[32 * KT_PER_BLOCK];
+    __shared__ int k_dh[32 * KT_PER_BLOCK], k_dw[32 * KT_PER_BLOCK];
+    const int b = blockIdx.z;
+    const int n0 = blockIdx.x * 32, kb0 = blockIdx.y * 32 * KT_PER_BLOCK;
+    const int N = g.Ho * g.Wo, kk = g.kH * g.kW, HW = g.H * g.W;
+    const int tid = threadIdx.y * 32 + threadIdx.x;
+    if (tid < 32 * KT_PER_BLOCK) {
+        const int k = kb0 + tid;
+        const int c = k / kk, tap = k - c * kk;
+        const int kh = tap / g.kW, kw = tap - kh * g.kW;
+        k_base[tid] = k < Kg ? (int64_t)c * HW : -1;  // -1: padding column k >= Kg
+        k_dh[tid] = kh * g.dH - g.pH;
+        k_dw[tid] = kw * g.dW - g.pW;
+    }
+    const float* xb = x + ((int64_t)b * g.C + c0) * HW;
+    const int n = n0 + threadIdx.x;
+    const int ho = n / g.Wo, wo = n - ho * g.Wo;
+    const int hs = ho * g.sH, ws = wo * g.sW;
+    __syncthreads();
+    for (int kt = 0; kt < KT_PER_BLOCK; ++kt) {
+        const int k0 = kb0 + kt * 32;
+        if (k0 >= Kp) break;  // block-uniform
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+            const int kl = kt * 32 + threadIdx.y + j;
+            const int64_t base = k_base[kl];
+            const int ih = hs + k_dh[kl], iw = ws + k_dw[kl];
+            float v = 0.0f;
+            if (base >= 0 && n < N && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W)
+                v = __ldg(xb + base + ih * g.W + iw);
+            tile[threadIdx.y + j][threadIdx.x] = v;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+            const int nn = n0 + threadIdx.y + j;
+            const int k = k0 + threadIdx.x;
+            if (nn < N && k < Kp) {
+                const float v = tile[threadIdx.x][threadIdx.y + j];
+                const float h = ptx::to_tf32(v);
+                const int64_t o = ((int64_t)b * N + nn) * Kp + k;
+                hi[o] = h;
+                lo[o] = ptx::to_tf32(v - h);
+            }
+        }
+        __syncthreads();  // the tile is refilled by the next k tile
+    }
+}
+
+// Weight-gradient operand: planes [r][Kp] with r = c*kk + tap (image channel
+// c0 + c) and K index k = b*N + n over batch x column pixels -- the batch-inner
+// column matrix, split as it is formed.  With a 1 x 1 geometry this is the
+// [B][C][N] -> [C][B*N] permute of the other operand.  One block row per r,
+// four consecutive k per thread (float4 stores).
+__global__ void im2col_split_rows_kernel(const float* __restrict__ x, const Geo g, int c0, int rows, int64_t BN,
+                                         int64_t Kp, float* __restrict__ hi, float* __restrict__ lo) {
+    const int r = blockIdx.y;
+    if (r >= rows) return;
+    const int N = g.Ho * g.Wo, kk = g.kH * g.kW, HW = g.H * g.W;
+    const int c = r / kk, tap = r - c * kk;
+    const int oh = (tap / g.kW) * g.dH - g.pH, ow = (tap % g.kW) * g.dW - g.pW;
+    const float* xc = x + (int64_t)(c0 + c) * HW;
+    const int64_t img = (int64_t)g.C * HW;
+    float* ho_ = hi + (int64_t)r * Kp;
+    float* lo_ = lo + (int64_t)r * Kp;
+    for (int64_t k4 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; k4 < Kp;
+         k4 += (int64_t)gridDim.x * blockDim.x * 4) {
+        float v[4];
+        // (b, h, w) of k4, then stepped along w without divisions
+        const int b0 = (int)(k4 / N);
+        const int n = (int)(k4 - (int64_t)b0 * N);
+        int b = b0, h = n / g.Wo, w = n - h * g.Wo;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[j] = 0.0f;
+            if (k4 + j < BN) {
+                const int ih = h * g.sH + oh, iw = w * g.sW + ow;
+                if ((unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W)
+                    v[j] = __ldg(xc + b * img + ih * g.W + iw);
+            }
+            if (++w == g.Wo) {
+                w = 0;
+                if (++h == g.Ho) {
+                    h = 0;
+                    ++b;
+                }
+            }
+        }
+        float hv[4], lv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            hv[j] = ptx::to_tf32(v[j]);
+            lv[j] = ptx::to_tf32(v[j] - hv[j]);
+        }
+        *reinterpret_cast<float4*>(ho_ + k4) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<float4*>(lo_ + k4) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+    }
+}
+
 // Grid of `rows` blocks as (x, y) with x <= 65535 * 1024.
 dim3 row_grid(int64_t rows) {
     const int64_t x = std::min<int64_t>(rows, 1 << 20);
@@ -181,6 +297,74 @@ jst_gemm_desc desc(int M, int N, int K, const float* A, int64_t lda, int64_t sA,
     return d;
 }
 
+// Whether the library's automatic choice puts this GEMM on the tensor-core kernel.
+bool on_tensor_cores(int M, int N, int K, int batch) {
+    jst_gemm_desc d;
+    jst_gemm_desc_init(&d, M, N, K, reinterpret_cast<const float*>(16), reinterpret_cast<const float*>(16),
+                       reinterpret_cast<float*>(16));
+    d.batch = batch;
+    d.strideA = (int64_t)M * K;
+    d.strideB = (int64_t)K * N;
+    d.strideC = (int64_t)M * N;
+    return jst_gemm_select_kernel(&d) == JST_KERNEL_TC3XTF32;
+}
+
+GemmArgs shape_args(int M, int N, int K, int batch) {
+    GemmArgs a{};
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.batch = batch;
+    return a;
+}
+
+int launch_im2col_split_rows(const float* x, const Geo& g, int c0, int rows, int64_t BN, int64_t Kp, float* hi,
+                             float* lo, cudaStream_t s) {
+    if (rows == 0 || Kp == 0) return JST_OK;
+    if (rows > 65535) return set_status(JST_ERR_UNSUPPORTED, "conv: more than 65535 column rows per group");
+    const int64_t want = (Kp / 4 + 255) / 256;
+    const int bx = (int)std::min<int64_t>(want, std::max<int64_t>(1, 148LL * 8 / rows + 1));
+    {
+        ProfScope prof(s, KID_CONV);
+        im2col_split_rows_kernel<<<dim3(bx, rows), 256, 0, s>>>(x, g, c0, rows, BN, Kp, hi, lo);
+    }
+    return cudaPeekAtLastError() == cudaSuccess ? JST_OK : set_status(JST_ERR_CUDA, "im2col split launch failed");
+}
+
+// Forward on the tensor-core kernel with im2col fused into the split of the
+// column operand; the weights are split once per group and broadcast over b.
+int conv2d_tc(const float* input, const float* weight, const float* bias, float* output, const Geo& g, int Co,
+              int groups, cudaStream_t s) {
+    const int Ci_g = g.C / groups, Co_g = Co / groups;
+    const int N = g.Ho * g.Wo, Kg = Ci_g * g.kH * g.kW, Kp = (Kg + 3) & ~3;
+    const size_t a_plane = (size_t)Co_g * Kp, b_plane = (size_t)g.B * N * Kp;
+    void* ws = nullptr;
+    int rc = workspace_alloc(2 * (a_plane + b_plane) * sizeof(float), s, &ws);
+    if (rc) return rc;
+    float* a_hi = static_cast<float*>(ws);
+    float* a_lo = a_hi + a_plane;
+    float* b_hi = a_lo + a_plane;
+    float* b_lo = b_hi + b_plane;
+    for (int grp = 0; grp < groups && !rc; ++grp) {
+        rc = tc_split(weight + (int64_t)grp * Co_g * Kg, 1, Kg, 0, Co_g, Kg, 1, a_hi, a_lo, s);
+        if (rc) break;
+        {
+            ProfScope prof(s, KID_CONV);
+            im2col_split_t_kernel<<<dim3((N + 31) / 32, (Kp + 32 * KT_PER_BLOCK - 1) / (32 * KT_PER_BLOCK), g.B),
+                                    dim3(32, 8), 0, s>>>(input, g, grp * Ci_g, Kg, Kp, b_hi, b_lo);
+        }
+        if (cudaPeekAtLastError() != cudaSuccess) {
+            rc = set_status(JST_ERR_CUDA, "im2col split launch failed");
+            break;
+        }
+        rc = tc_gemm_planes(a_hi, a_lo, b_hi, b_lo, Co_g, N, Kg, g.B, output + (int64_t)grp * Co_g * N, N,
+                            (int64_t)Co * N, bias ? bias + (int64_t)grp * Co_g : nullptr, 0, device_error_word(), s,
+                            0, nullptr, 0, 0, /*bias_row=*/bias ? 1 : 0, /*a_bcast=*/1, /*b_bcast=*/0, /*kslices=*/1);
+    }
+    const int frc = workspace_free(ws, s);
+    return rc ? rc : frc;
+}
+
 // Conv2d forward (conv.cu:402-434): out[b, g] = W_g . col[b, g] (+ bias), batched over b.
 int conv2d(const float* input, const float* weight, const float* bias, float* output, float* col_buf, int B, int Ci,
            int H, int W, int Co, int kH, int kW, int sH, int sW, int pH, int pW, int dH, int dW, int groups, int Ho,
@@ -191,6 +375,12 @@ int conv2d(const float* input, const float* weight, const float* bias, float* ou
     const int64_t N = (int64_t)Ho * Wo, kk = (int64_t)kH * kW, Kg = Ci_g * kk;
     if (!fits_int(N) || !fits_int(Kg)) return set_status(JST_ERR_ARG, "conv: GEMM dimension exceeds int");
     const bool direct = kH == 1 && kW == 1 && sH == 1 && sW == 1 && pH == 0 && pW == 0 && Ho == H && Wo == W;
+    if (!direct && B > 0 && B <= 65535 && Co_g > 0 && Kg > 0 && on_tensor_cores(Co_g, (int)N, (int)Kg, B) &&
+        tc_split_k(shape_args(Co_g, (int)N, (int)Kg, B)) == 1) {
+        rc = conv2d_tc(input, weight, bias, output, Geo{B, Ci, H, W, kH, kW, sH, sW, pH, pW, dH, dW, Ho, Wo}, Co,
+                       groups, s);
+        return rc ? rc : set_status(JST_OK, nullptr);
+    }
     const float* col = input;
     if (!direct) {
         if (!col_buf) return set_status(JST_ERR_ARG, "conv: null col_buf");
@@ -233,6 +423,58 @@ int conv_transpose2d(const float* input, const float* weight, const float* bias,
     return rc ? rc : set_status(JST_OK, nullptr);
 }
 
+// Weight gradient on the tensor-core kernel: both operands are K-major rows
+// over K = B*N and are split as they are gathered (the permute of rows_src and
+// the batch-inner im2col of col_src), so neither the permuted copy nor the
+// column matrix is written.  K is usually long and the output small, so the
+// product is split over K when the tiles cannot fill the SMs.
+int backward_weight_tc(const float* rows_src, int Prows, const float* col_src, const Geo& cg, float* grad_weight,
+                       int groups, cudaStream_t s) {
+    const int B = cg.B, N = cg.Ho * cg.Wo;
+    const int64_t BN = (int64_t)B * N, Kp = (BN + 3) & ~int64_t(3);
+    const int Pg = Prows / groups, Cg = cg.C / groups, Qg = Cg * cg.kH * cg.kW;
+    const int S = tc_split_k(shape_args(Pg, Qg, (int)BN, 1));
+    const size_t p_plane = (size_t)Pg * Kp, q_plane = (size_t)Qg * Kp, part = S > 1 ? (size_t)S * Pg * Qg : 0;
+    void* ws = nullptr;
+    int rc = workspace_alloc((2 * (p_plane + q_plane) + part) * sizeof(float), s, &ws);
+    if (rc) return rc;
+    float* p_hi = static_cast<float*>(ws);
+    float* p_lo = p_hi + p_plane;
+    float* q_hi = p_lo + p_plane;
+    float* q_lo = q_hi + q_plane;
+    float* pt = q_lo + q_plane;
+    // rows_src [B][Prows][N] as a 1 x 1 "image" of N pixels: its im2col rows are the permute
+    const Geo pg{B, Prows, 1, N, 1, 1, 1, 1, 0, 0, 1, 1, 1, N};
+    for (int grp = 0; grp < groups && !rc; ++grp) {
+        rc = launch_im2col_split_rows(rows_src, pg, grp * Pg, Pg, BN, Kp, p_hi, p_lo, s);
+        if (!rc) rc = launch_im2col_split_rows(col_src, cg, grp * Cg, Qg, BN, Kp, q_hi, q_lo, s);
+        if (rc) break;
+        float* gw = grad_weight + (int64_t)grp * Pg * Qg;
+        if (S <= 1) {
+            rc = tc_gemm_planes(p_hi, p_lo, q_hi, q_lo, Pg, Qg, (int)BN, 1, gw, Qg, (int64_t)Pg * Qg, nullptr, 0,
+                                device_error_word(), s);
+        } else {
+            rc = tc_gemm_planes(p_hi, p_lo, q_hi, q_lo, Pg, Qg, (int)BN, 1, pt, Qg, (int64_t)Pg * Qg, nullptr, 0,
+                                device_error_word(), s, 0, nullptr, 0, 0, 0, 0, 0, S);
+            if (!rc) {
+                SplitKReduce r{};
+                r.part = pt;
+                r.slices = S;
+                r.batch = 1;
+                r.M = Pg;
+                r.N = Qg;
+                r.C = gw;
+                r.ldc = Qg;
+                r.strideC = (int64_t)Pg * Qg;
+                r.vecC = (reinterpret_cast<uintptr_t>(gw) & 15) == 0 && (Qg % 4) == 0;
+                rc = splitk_reduce_run(r, s);
+            }
+        }
+    }
+    const int frc = workspace_free(ws, s);
+    return rc ? rc : frc;
+}
+
 // grad_weight[g] = P[g] . Q[g]^T over K = B*N, where P = rows_src permuted to
 // [rows][B*N] and Q = im2col(col_src) batch-inner (conv.cu:495-627).
 //   P: [Prows][B*N]  (group g: rows g*Pg ..)
@@ -246,6 +488,10 @@ int backward_weight(const float* rows_src, int Prows, const float* col_src, cons
     const int Pg = Prows / groups;
     const int64_t Qg = (int64_t)(cg.C / groups) * kk;
     if (!fits_int(BN) || !fits_int(Qg)) return set_status(JST_ERR_ARG, "conv: GEMM dimension exceeds int");
+    if (Pg > 0 && Qg > 0 && BN > 0 && Pg <= 65535 && Qg <= 65535 && on_tensor_cores(Pg, (int)Qg, (int)BN, groups)) {
+        const int rc = backward_weight_tc(rows_src, Prows, col_src, cg, grad_weight, groups, s);
+        return rc ? rc : set_status(JST_OK, nullptr);
+    }
     if (!col_buf) return set_status(JST_ERR_ARG, "conv: null col_buf");
     int rc = im2col(col_src, col_buf, cg, true, s);
     if (rc) return rc;

@@ -208,8 +208,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                          ((p.strideC & 3) == 0);
         float* stg = reinterpret_cast<float*>(smem + RING_BYTES + 256) + (warp - 2) * (32 * STG_LD);
         // a row bias is added in registers before epi(); epi() then sees no column bias
+        const bool row_bias = p.bias_row && p.bias;
         const float* cbias = p.bias_row ? nullptr : p.bias;
-        const float rbias = (p.bias_row && row < p.M) ? __ldg(p.bias + row) : 0.0f;
+        const float rbias = (row_bias && row < p.M) ? __ldg(p.bias + row) : 0.0f;
         if (ok) {
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
@@ -222,7 +223,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ptx::tmem_ld_wait();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(rl[j]));
-                if (p.bias_row) {
+                if (row_bias) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + rbias);
                 }

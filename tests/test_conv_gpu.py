@@ -78,6 +78,8 @@ CASES2D = [
     (2, 6, 6, 9, 10, (5, 3), (3, 2), (2, 1), (2, 1), 6),      # depthwise-like
     (1, 5, 7, 1, 40, (1, 4), (1, 3), (0, 2), (1, 2), 1),      # H = 1
     (16, 64, 128, 32, 32, (3, 3), (1, 1), (1, 1), (1, 1), 1),  # large enough for the tensor-core kernel
+    (32, 128, 128, 32, 32, (3, 3), (1, 1), (1, 1), (1, 1), 2),  # tensor cores, two groups
+    (16, 64, 128, 63, 64, (3, 3), (2, 2), (1, 1), (1, 1), 1),  # tensor cores, stride 2, ragged pixel count
 ]
 
 
