@@ -159,6 +159,24 @@ int jst_matmul_host(const float* a, const float* b, float* c, int M, int K, int 
  */
 int jst_matmul_host_async(const float* a, const float* b, float* c, int M, int K, int N, jst_stream_t stream);
 
+/* ------------------------------------------ host <-> device transfers */
+/*
+ * The copies either side of the path: what Tensor::from_array / from_buffer
+ * (native/core/tensor.cpp:740-750, a synchronous pageable cudaMemcpy) and
+ * Tensor::to_array (tensor.cpp:775-800, cudaDeviceSynchronize + copy) do, for
+ * an N-API shim that passes the Float32Array's storage directly.
+ * Pageable host memory is staged through two pinned 8 MiB chunks per device
+ * (host copy of one chunk overlapping the DMA of the other); page-locked host
+ * memory is copied by one direct DMA.
+ *   jst_copy_h2d: returns once `src_host` has been read (the caller may reuse
+ *     it); the device data is ready in `stream` order.
+ *   jst_copy_d2h: ordered after earlier work on `stream`; waits for that
+ *     stream only, and returns when `dst_host` holds the data.
+ * Calls on one device share its staging chunks and are serialised.
+ */
+int jst_copy_h2d(void* dst_device, const void* src_host, size_t bytes, jst_stream_t stream);
+int jst_copy_d2h(void* dst_host, const void* src_device, size_t bytes, jst_stream_t stream);
+
 /* ---------------------------------------------------- device-side status */
 /*
  * Kernels never trap: a pipeline wait that exceeds its bound sets a device
@@ -167,7 +185,8 @@ int jst_matmul_host_async(const float* a, const float* b, float* c, int M, int K
  */
 int jst_device_error(void);
 
-/* Release cached device workspace and pinned staging buffers of this process. */
+/* Release cached device workspace and pinned staging buffers of this process
+ * (including the jst_copy_h2d / jst_copy_d2h staging chunks). */
 void jst_release_caches(void);
 
 /* ------------------------------------------------------------ profiling */

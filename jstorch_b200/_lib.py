@@ -87,6 +87,10 @@ def load() -> ctypes.CDLL:
     lib.jst_matmul_host.argtypes = [fp, fp, fp, ci, ci, ci]
     lib.jst_matmul_host_async.restype = ci
     lib.jst_matmul_host_async.argtypes = [fp, fp, fp, ci, ci, ci, vp]
+    lib.jst_copy_h2d.restype = ci
+    lib.jst_copy_h2d.argtypes = [vp, vp, ctypes.c_size_t, vp]
+    lib.jst_copy_d2h.restype = ci
+    lib.jst_copy_d2h.argtypes = [vp, vp, ctypes.c_size_t, vp]
     lib.jst_device_error.restype = ci
     lib.jst_device_error.argtypes = []
     lib.jst_release_caches.restype = None

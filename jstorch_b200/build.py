@@ -34,7 +34,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
            "--expt-relaxed-constexpr", "-DNDEBUG", f"-I{INCLUDE}"] + ARCH
 
-GEMM_SOURCES = ["gemm_api.cu", "gemm_ffma.cu", "gemm_tc.cu", "splitk.cu", "conv.cu", "profile.cu"]
+GEMM_SOURCES = ["gemm_api.cu", "gemm_ffma.cu", "gemm_tc.cu", "splitk.cu", "conv.cu", "hostio.cu", "profile.cu"]
 GEMM_HEADERS = ["gemm_internal.h", "ptx.cuh"]
 GEMM_LIB = PKG / "libjstorch_gemm.so"
 
@@ -77,9 +77,9 @@ def build_gemm(force: bool = False, ptxas_v: bool = False, verbose: bool = False
 
 
 CORE = CSRC / "core"
-CORE_CPP = ["tensor.cpp", "autograd.cpp", "allocator.cpp", "compiled.cpp", "hostio.cpp", "binding.cpp"]
+CORE_CPP = ["tensor.cpp", "autograd.cpp", "allocator.cpp", "compiled.cpp", "binding.cpp"]
 CORE_CU = ["kernels.cu"]
-CORE_HEADERS = ["tensor.h", "autograd.h", "allocator.h", "compiled.h", "hostio.h", "core_kernels.h"]
+CORE_HEADERS = ["tensor.h", "autograd.h", "allocator.h", "compiled.h", "core_kernels.h"]
 CORE_EXT = PKG / ("_core" + sysconfig.get_config_var("EXT_SUFFIX"))
 CXX = os.environ.get("CXX", "g++")
 

@@ -9,7 +9,7 @@
 
 #include "autograd.h"
 #include "compiled.h"
-#include "hostio.h"
+#include "../../../include/jstorch_gemm.h"
 #include "core_kernels.h"
 
 namespace py = pybind11;
@@ -144,5 +144,6 @@ PYBIND11_MODULE(_core, m) {
     m.def("stridedCopies", &jst::core::strided_copy_count,
           "number of contiguous() materialisations (strided copies) so far");
     m.def("cachedBytes", &jst::core::cached_bytes);
-    m.def("releaseHostStaging", &jst::core::hostio_release, "free the pinned fromBuffer / toArray staging");
+    m.def("releaseHostStaging", [] { jst_release_caches(); },
+          "free the pinned fromBuffer / toArray staging (and the GEMM library's other caches)");
 }

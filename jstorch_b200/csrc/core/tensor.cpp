@@ -1,8 +1,6 @@
 // tensor.cpp -- host core Tensor (see tensor.h).
 #include "tensor.h"
 
-#include "hostio.h"
-
 #include <algorithm>
 #include <atomic>
 #include <numeric>
@@ -145,7 +143,9 @@ bool Tensor::is_contiguous() const {
 Tensor Tensor::from_buffer(const float* host, int64_t count, const Shape& shape) {
     if (numel(shape) != count) throw std::runtime_error("from_buffer: size mismatch");
     Tensor r(shape);
-    h2d(r.data(), host, count, g_stream);  // pinned, double-buffered staging (hostio.h)
+    // pinned, double-buffered staging (jst_copy_h2d); ready in core-stream order
+    if (jst_copy_h2d(r.data(), host, (size_t)count * sizeof(float), reinterpret_cast<jst_stream_t>(g_stream)) != JST_OK)
+        throw std::runtime_error(std::string("fromBuffer: ") + jst_last_error());
     return r;
 }
 
@@ -172,7 +172,10 @@ std::vector<float> Tensor::to_array() const {
 void Tensor::to_host(float* dst) const {
     if (size() == 0) return;
     const Tensor c = contiguous();  // strided views are gathered on the device first
-    d2h(dst, c.data(), c.size(), g_stream);  // waits for the core stream only
+    // waits for the core stream only
+    if (jst_copy_d2h(dst, c.data(), (size_t)c.size() * sizeof(float), reinterpret_cast<jst_stream_t>(g_stream)) !=
+        JST_OK)
+        throw std::runtime_error(std::string("toArray: ") + jst_last_error());
 }
 
 Tensor Tensor::contiguous() const {

@@ -461,6 +461,7 @@ void jst_release_caches(void) {
         if (jst::g_dev[i].pool) cudaMemPoolTrimTo(jst::g_dev[i].pool, 0);
     }
     cudaSetDevice(cur);
+    jst::hostio_release();
 }
 
 }  // extern "C"

@@ -69,6 +69,9 @@ size_t ffma_workspace_bytes(const GemmArgs& a);
 // K == 0: C = epilogue(0)
 int fill_epilogue_run(const GemmArgs& a, cudaStream_t s);
 
+// Free the pinned staging of jst_copy_h2d / jst_copy_d2h (hostio.cu).
+int hostio_release();
+
 // Reduce of a split-K GEMM (splitk.cu): C = epilogue(sum over slices of part).
 struct SplitKReduce {
     const float* part;  // [slices][batch][M][N] packed

@@ -1,26 +1,51 @@
-// hostio.cpp -- pinned, double-buffered host <-> device copies (see hostio.h).
-#include "hostio.h"
+// hostio.cu -- jst_copy_h2d / jst_copy_d2h: host <-> device copies through
+// pinned, double-buffered staging (include/jstorch_gemm.h).
+//
+// Reference: Tensor::from_array / from_buffer (native/core/tensor.cpp:740-750)
+// is a synchronous cudaMemcpy from the JS heap (pageable), and to_array
+// (:775-800) synchronises the whole device, copies synchronously, and then
+// napi.cpp:17-30 builds nested JS arrays element by element.
+//
+// Here, per device, two pinned staging chunks alternate: the host copy of
+// chunk i+1 (pageable -> pinned, split over a few worker threads) runs while
+// the DMA of chunk i is in flight.
+//   * h2d returns once the source has been read; the last DMAs may still be
+//     running on the stream (they read only the staging chunks), so the data
+//     is ready in stream order, not at return;
+//   * d2h waits for its stream only (not the whole device) and returns when
+//     the destination holds the data;
+//   * a source or destination that is already page-locked is copied by one
+//     direct DMA.
+#include <cuda_runtime.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <condition_variable>
+#include <cstdint>
 #include <cstring>
 #include <mutex>
-#include <stdexcept>
-#include <string>
 #include <thread>
 #include <vector>
 
-#include <unistd.h>
+#include "gemm_internal.h"
 
 namespace jst {
-namespace core {
+namespace io {
 
 namespace {
+
+constexpr size_t kStageChunkBytes = 8u << 20;  // per staging chunk
+
+// CUDA error -> exception inside this file; the C entry points turn it into a status.
+struct CudaFail {
+    const char* what;
+    cudaError_t err;
+};
 
 void ck(cudaError_t e, const char* what) {
     if (e != cudaSuccess) {
         cudaGetLastError();
-        throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+        throw CudaFail{what, e};
     }
 }
 
@@ -37,7 +62,7 @@ Stage g_stage[kMaxDevices];
 Stage& stage_for_current_device() {
     int dev = 0;
     ck(cudaGetDevice(&dev), "cudaGetDevice");
-    if (dev < 0 || dev >= kMaxDevices) throw std::runtime_error("hostio: device index out of range");
+    if (dev < 0 || dev >= kMaxDevices) throw CudaFail{"device index out of range", cudaErrorInvalidDevice};
     return g_stage[dev];
 }
 
@@ -153,9 +178,8 @@ CopyPool& copy_pool() {
 
 }  // namespace
 
-void h2d(float* dst, const float* src, int64_t count, cudaStream_t s) {
-    if (count <= 0) return;
-    const size_t bytes = (size_t)count * sizeof(float);
+void h2d(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+    if (bytes == 0) return;
     if (is_pinned(src)) {
         // Direct DMA; wait for it, because the caller may reuse its buffer on return.
         ck(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s), "H2D copy");
@@ -182,9 +206,8 @@ void h2d(float* dst, const float* src, int64_t count, cudaStream_t s) {
     }
 }
 
-void d2h(float* dst, const float* src, int64_t count, cudaStream_t s) {
-    if (count <= 0) return;
-    const size_t bytes = (size_t)count * sizeof(float);
+void d2h(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+    if (bytes == 0) return;
     if (is_pinned(dst) || bytes <= kDirectBytes) {
         ck(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s), "D2H copy");
         ck(cudaStreamSynchronize(s), "D2H wait");
@@ -217,7 +240,7 @@ void d2h(float* dst, const float* src, int64_t count, cudaStream_t s) {
     }
 }
 
-void hostio_release() {
+void release() {
     for (int d = 0; d < kMaxDevices; ++d) {
         Stage& st = g_stage[d];
         std::lock_guard<std::mutex> lk(st.mu);
@@ -236,5 +259,35 @@ void hostio_release() {
     }
 }
 
-}  // namespace core
+}  // namespace io
+
+int hostio_release() {
+    io::release();
+    return JST_OK;
+}
+
 }  // namespace jst
+
+extern "C" {
+
+int jst_copy_h2d(void* dst_device, const void* src_host, size_t bytes, jst_stream_t stream) {
+    if (bytes && (!dst_device || !src_host)) return jst::set_status(JST_ERR_ARG, "jst_copy_h2d: null pointer");
+    try {
+        jst::io::h2d(dst_device, src_host, bytes, reinterpret_cast<cudaStream_t>(stream));
+    } catch (const jst::io::CudaFail& f) {
+        return jst::set_status(f.err == cudaErrorMemoryAllocation ? JST_ERR_NOMEM : JST_ERR_CUDA, f.what);
+    }
+    return jst::set_status(JST_OK, nullptr);
+}
+
+int jst_copy_d2h(void* dst_host, const void* src_device, size_t bytes, jst_stream_t stream) {
+    if (bytes && (!dst_host || !src_device)) return jst::set_status(JST_ERR_ARG, "jst_copy_d2h: null pointer");
+    try {
+        jst::io::d2h(dst_host, src_device, bytes, reinterpret_cast<cudaStream_t>(stream));
+    } catch (const jst::io::CudaFail& f) {
+        return jst::set_status(f.err == cudaErrorMemoryAllocation ? JST_ERR_NOMEM : JST_ERR_CUDA, f.what);
+    }
+    return jst::set_status(JST_OK, nullptr);
+}
+
+}  // extern "C"

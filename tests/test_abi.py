@@ -59,6 +59,13 @@ def test_conv_argument_validation_without_gpu():
     assert lib.jst_get_last_status() == 1
 
 
+def test_copy_entry_points_validate_without_gpu():
+    lib = _lib.load()
+    assert lib.jst_copy_h2d(None, None, 16, None) == 1  # JST_ERR_ARG: null pointers
+    assert lib.jst_copy_d2h(None, None, 16, None) == 1
+    assert b"null" in lib.jst_last_error()
+
+
 def test_desc_layout_matches_c():
     # jst_gemm_desc_init writes through the C struct; the ctypes mirror must
     # read back the same fields

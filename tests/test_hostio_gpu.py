@@ -71,3 +71,19 @@ def test_ordering_with_gemm(core):
     ref = oracle.gemm_f64(A, B, rows=np.arange(0, 1024, 37))
     err, _ = oracle.max_rel_err(A, B, C, ref, rows=np.arange(0, 1024, 37))
     assert err <= 2e-6
+
+
+def test_c_abi_copies_on_torch_buffers():
+    """jst_copy_h2d / jst_copy_d2h directly: odd byte counts, a pageable numpy
+    source and destination, and a stream other than the legacy one."""
+    import torch
+    from jstorch_b200 import _lib
+    lib = _lib.load()
+    s = torch.cuda.Stream()
+    for nbytes in (1, 4097, 3 * (8 << 20) + 5):
+        src = np.random.default_rng(nbytes).integers(0, 256, nbytes, dtype=np.uint8)
+        dev = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        _lib.check(lib.jst_copy_h2d(dev.data_ptr(), src.ctypes.data, nbytes, s.cuda_stream))
+        back = np.empty(nbytes, dtype=np.uint8)
+        _lib.check(lib.jst_copy_d2h(back.ctypes.data, dev.data_ptr(), nbytes, s.cuda_stream))
+        assert np.array_equal(back, src)
