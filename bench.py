@@ -646,6 +646,54 @@ def run_config(args) -> None:
                                 "reference_design_tf32_ms": refd, "reference_design_tf32_tflops": tf(refd)},
                     "note": "context rows: torch cuDNN conv2d with TF32 off; the reference's im2col + per-image "
                             "GEMM loop restated with torch (TF32 on, as conv.cu:190-196)"})
+    elif args.config == 8:
+        # GRU forward (src/nn.js:451-536) through jst_gru_layer_forward: seq 64, batch 64,
+        # 512 -> 1024 hidden, 2 layers
+        from jstorch_b200.rnn import GRU
+
+        seq, batch, inp, H, layers = 64, 64, 512, 1024, 2
+        gen = torch.Generator(device=dev).manual_seed(8)
+        gru = GRU(inp, H, layers, generator=gen)
+        x = torch.randn((seq, batch, inp), device=dev, generator=gen)
+        flops = sum(2.0 * seq * batch * 3 * H * ((inp if l == 0 else H) + H) for l in range(layers))
+        _lib.profile_enable(True)
+        ms = _time_device(lambda: gru(x), args.steps, args.warmup, stream)
+        ks = _lib.profile_read()
+        _lib.profile_enable(False)
+
+        def ref_design():  # nn.js:477-511 op by op: per step two matmuls + the gate ops, TF32 as the reference
+            h_in = x
+            for l in range(layers):
+                p = gru.params
+                wih, whh = p[f"weight_ih_l{l}"], p[f"weight_hh_l{l}"]
+                bih, bhh = p[f"bias_ih_l{l}"], p[f"bias_hh_l{l}"]
+                h = torch.zeros((batch, H), device=dev)
+                outs = []
+                for t in range(seq):
+                    gi = h_in[t].matmul(wih.t()).add(bih)
+                    gh = h.matmul(whh.t()).add(bhh)
+                    r = gi[:, :H].add(gh[:, :H]).sigmoid()
+                    z = gi[:, H:2 * H].add(gh[:, H:2 * H]).sigmoid()
+                    n = gi[:, 2 * H:].add(r.mul(gh[:, 2 * H:])).tanh()
+                    h = z.mul(-1).add(1).mul(n).add(z.mul(h))
+                    outs.append(h.unsqueeze(0))
+                h_in = torch.cat(outs, 0)
+            return h_in
+
+        torch.backends.cuda.matmul.allow_tf32 = True
+        refd = _time_device(ref_design, args.steps, args.warmup, stream)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        torch.backends.cudnn.allow_tf32 = False
+        tg = torch.nn.GRU(inp, H, layers).to(dev)
+        with torch.no_grad():
+            cudnn = _time_device(lambda: tg(x), args.steps, args.warmup, stream)
+        tf = lambda t: flops / (t * 1e-3) / 1e12
+        out.update({"metric": "GRU forward, seq 64, batch 64, 512->1024, 2 layers", "unit": "ms", "value": ms,
+                    "higher_is_better": False, "tflops": tf(ms),
+                    "kernels": {k: {"launches": v[0], "ms": v[1]} for k, v in ks.items()},
+                    "context": {"reference_design_tf32_ms": refd, "cudnn_fp32_ms": cudnn},
+                    "note": "context rows: the reference's per-step JS op sequence restated with torch "
+                            "(TF32 on, as matmul.cu:12); torch.nn.GRU (cuDNN) with TF32 off"})
     print(json.dumps(out), flush=True)
 
 
@@ -760,7 +808,7 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
     ap.add_argument("--size", type=int, default=SIZE, help="square GEMM size at N=1 (default 8192)")
-    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5, 6, 7],
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5, 6, 7, 8],
                     help="secondary measurement of one BASELINE configuration (0: the headline line)")
     ap.add_argument("--trace", action="store_true", help="N>1: add one traced step's timeline to the line")
     ap.add_argument("--c-gather", choices=["auto", "multicast", "copy", "nccl"], default="auto",

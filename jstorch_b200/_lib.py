@@ -14,6 +14,7 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libjstorch_gemm.so"
 HEADER = PKG.parent / "include" / "jstorch_gemm.h"
 CONV_HEADER = PKG.parent / "include" / "jstorch_conv.h"
+RNN_HEADER = PKG.parent / "include" / "jstorch_rnn.h"
 
 JST_OK = 0
 STATUS_NAMES = {
@@ -116,6 +117,8 @@ def load() -> ctypes.CDLL:
     for name in ("launch_conv2d_backward_weight", "launch_conv_transpose2d_backward_weight"):
         getattr(lib, name).restype = None
         getattr(lib, name).argtypes = [vp] * 4 + [ci] * 16 + [vp]
+    lib.jst_gru_layer_forward.restype = ci
+    lib.jst_gru_layer_forward.argtypes = [vp, ci, ci, ci, ci, vp, vp, vp, vp, vp, ci, vp, ctypes.c_int64, vp, vp]
     _lib = lib
     return lib
 

@@ -34,7 +34,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVFLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
            "--expt-relaxed-constexpr", "-DNDEBUG", f"-I{INCLUDE}"] + ARCH
 
-GEMM_SOURCES = ["gemm_api.cu", "gemm_ffma.cu", "gemm_tc.cu", "splitk.cu", "conv.cu", "hostio.cu", "profile.cu"]
+GEMM_SOURCES = ["gemm_api.cu", "gemm_ffma.cu", "gemm_tc.cu", "splitk.cu", "conv.cu", "gru.cu", "hostio.cu", "profile.cu"]
 GEMM_HEADERS = ["gemm_internal.h", "ptx.cuh"]
 GEMM_LIB = PKG / "libjstorch_gemm.so"
 
@@ -60,7 +60,7 @@ def _run(cmd: list[str], verbose: bool) -> None:
 
 def build_gemm(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> Path:
     BUILD.mkdir(exist_ok=True)
-    headers = [CSRC / h for h in GEMM_HEADERS] + [INCLUDE / "jstorch_gemm.h", INCLUDE / "jstorch_conv.h"]
+    headers = [CSRC / h for h in GEMM_HEADERS] + [INCLUDE / "jstorch_gemm.h", INCLUDE / "jstorch_conv.h", INCLUDE / "jstorch_rnn.h"]
     objs = []
     for src in GEMM_SOURCES:
         s = CSRC / src

@@ -96,6 +96,7 @@ enum KernelId {
     KID_FILL,
     KID_CONV,  // im2col / col2im / permute of the convolution launchers
     KID_SPLITK_REDUCE,
+    KID_RNN,  // GRU gate kernel
     KERNEL_ID_COUNT
 };
 

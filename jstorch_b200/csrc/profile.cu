@@ -34,7 +34,7 @@ std::vector<cudaEvent_t> g_free_events;
 Stat g_stats[KERNEL_ID_COUNT];
 
 const char* kKernelNames[KERNEL_ID_COUNT] = {"tc_gemm", "split_rows", "split_transpose", "ffma_gemm",
-                                             "fill_epilogue", "conv_im2col", "splitk_reduce"};
+                                             "fill_epilogue", "conv_im2col", "splitk_reduce", "gru_gate"};
 
 cudaEvent_t take_event() {
     if (!g_free_events.empty()) {

@@ -11,6 +11,7 @@ product (jstorch_b200) never calls it.
   conv2d_f64 / conv_transpose2d_f64 /      fp64 restatements of the im2col-GEMM
   conv2d_backward_weight_f64 /             convolution launchers (1-D = 2-D
   conv_transpose2d_backward_weight_f64     with H = 1), tap by tap
+  gru_forward_f64                          fp64 restatement of the reference's GRU
 
 Reference citations are relative to the JsTorch project root.
 """
@@ -307,3 +308,49 @@ def conv_transpose2d_backward_weight_f64(x, go, kernel, stride=(1, 1), padding=(
                 gw[g * Cig:(g + 1) * Cig, :, kh, kw] = np.einsum(
                     "bchw,bohw->co", xg, _taps(gg, kh, kw, dH, dW, sH, sW, Hi, Wi), optimize=True)
     return gw
+
+
+# --------------------------------------------------------------------- GRU
+def gru_forward_f64(x, params, hidden, num_layers=1, bidirectional=False, h0=None):
+    """The reference GRU (src/nn.js:451-536) in fp64, batch_first = False.
+
+    x [seq, batch, in]; params: dict with the PyTorch names weight_ih_l{l}[_reverse]
+    [3H, in], weight_hh_l{l} [3H, H], bias_ih_l{l}, bias_hh_l{l} [3H];
+    h0 [layers*dirs, batch, H] or None (zeros, nn.js:494).
+      _cell          nn.js:477-485  gi = x W_ih^T + b_ih, gh = h W_hh^T + b_hh,
+                                    r = sig(gi_r + gh_r), z = sig(gi_z + gh_z),
+                                    n = tanh(gi_n + r gh_n), h' = (1 - z) n + z h
+      _run_direction nn.js:487-511  reverse walks t = seq-1..0, output row t stays at t
+      forward        nn.js:513-535  layer input = previous output (directions
+                                    concatenated on features), h_n stacked per layer/direction
+    Returns (output [seq, batch, H*dirs], h_n [layers*dirs, batch, H])."""
+    x = np.asarray(x, np.float64)
+    seq, batch = x.shape[0], x.shape[1]
+    sig = lambda v: 1.0 / (1.0 + np.exp(-v))
+    dirs = 2 if bidirectional else 1
+    inp = x
+    hn = []
+    for l in range(num_layers):
+        outs = []
+        for d in range(dirs):
+            sfx = "_reverse" if d else ""
+            wih = np.asarray(params[f"weight_ih_l{l}{sfx}"], np.float64)
+            whh = np.asarray(params[f"weight_hh_l{l}{sfx}"], np.float64)
+            bih = np.asarray(params[f"bias_ih_l{l}{sfx}"], np.float64)
+            bhh = np.asarray(params[f"bias_hh_l{l}{sfx}"], np.float64)
+            H = hidden
+            h = np.zeros((batch, H)) if h0 is None else np.asarray(h0[l * dirs + d], np.float64)
+            out = np.zeros((seq, batch, H))
+            steps = range(seq - 1, -1, -1) if d else range(seq)
+            for t in steps:
+                gi = inp[t] @ wih.T + bih
+                gh = h @ whh.T + bhh
+                r = sig(gi[:, :H] + gh[:, :H])
+                z = sig(gi[:, H:2 * H] + gh[:, H:2 * H])
+                n = np.tanh(gi[:, 2 * H:] + r * gh[:, 2 * H:])
+                h = (1 - z) * n + z * h
+                out[t] = h
+            outs.append(out)
+            hn.append(h)
+        inp = np.concatenate(outs, axis=2)
+    return inp, np.stack(hn)

@@ -110,3 +110,13 @@ def test_no_device_is_an_error_not_a_fallback():
     d = _lib.GemmDesc()
     lib.jst_gemm_desc_init(ctypes.byref(d), 4, 4, 4, 0x1000, 0x2000, 0x3000)
     assert lib.jst_gemm_ex(ctypes.byref(d)) == 8  # JST_ERR_NO_DEVICE
+
+
+def test_rnn_header_exported_and_validates_without_gpu():
+    names = _lib.header_functions(_lib.RNN_HEADER)
+    assert names == ["jst_gru_layer_forward"]
+    lib = _lib.load()
+    assert hasattr(lib, "jst_gru_layer_forward")
+    # ld_out < hidden and a negative size are rejected on the host
+    assert lib.jst_gru_layer_forward(16, 2, 2, 4, 8, 16, 16, None, None, None, 0, 16, 4, None, None) == 1
+    assert lib.jst_gru_layer_forward(16, -1, 2, 4, 8, 16, 16, None, None, None, 0, 16, 8, None, None) == 1

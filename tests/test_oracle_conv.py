@@ -65,3 +65,4 @@ def test_output_sizes():
     assert oracle.conv_out_size(10, 3, 1, 0, 2) == 6
     assert oracle.conv_transpose_out_size(16, 4, 2, 1, 1) == 32
     assert oracle.conv_transpose_out_size(5, 3, 2, 0, 1, 1) == 12
+
