@@ -598,10 +598,38 @@ def run_config(args) -> None:
         r_up = wall(lambda: (dst.copy_(src), torch.cuda.synchronize()))
         r_dn = wall(lambda: dst.cpu())
         gbs = lambda t: nbytes / t / 1e9
+
+        # .bin model load (loader.js:18-44): 16 tensors of 16 MiB from a file in the page cache
+        import tempfile
+
+        from jstorch_b200 import loader
+        with tempfile.TemporaryDirectory() as td:
+            path = f"{td}/model.bin"
+            parts = {f"layer{i}.weight": flat[i * (1 << 22):(i + 1) * (1 << 22)].reshape(2048, 2048)
+                     for i in range(16)}
+            loader.save_model(path, parts, {"layers": 16})
+            t_load = wall(lambda: holder.__setitem__("m", loader.load_model(path)))
+
+            def ref_load():  # one synchronous pageable copy per tensor, as loader.js:41 -> fromBuffer
+                state = {}
+                with open(path, "rb") as f:
+                    buf = bytearray(f.read())  # fs.readFileSync
+                _, _, hdr, d0 = loader.read_header(buf)
+                for k, info in hdr["tensors"].items():
+                    a = np.frombuffer(buf, np.float32, info["size"], d0 + info["offset"]).reshape(info["shape"])
+                    state[k] = torch.from_numpy(a).to(dev)
+                torch.cuda.synchronize()
+                return state
+
+            t_rload = wall(ref_load)
+        holder.clear()
         out.update({"metric": "host I/O: Tensor.fromBuffer / toFloat32Array of a 256 MiB operand", "unit": "GB/s",
                     "value": gbs(t_up), "fromBuffer_gbs": gbs(t_up), "toArray_gbs": gbs(t_dn),
-                    "pageable_sync_reference_style": {"h2d_gbs": gbs(r_up), "d2h_gbs": gbs(r_dn)},
-                    "note": "wall clock per call incl. completion; pageable numpy source / destination"})
+                    "loadModel_gbs": gbs(t_load),
+                    "pageable_sync_reference_style": {"h2d_gbs": gbs(r_up), "d2h_gbs": gbs(r_dn),
+                                                      "loadModel_gbs": gbs(t_rload)},
+                    "note": "wall clock per call incl. completion; pageable numpy source / destination; "
+                            "loadModel: 256 MiB .bin of 16 tensors from the page cache"})
     elif args.config == 7:
         # conv2d through the im2col-GEMM launchers (conv.cu:402, :530): a 3x3, 256 -> 256
         # channel layer on 56 x 56 images, batch 32

@@ -89,7 +89,8 @@ PYBIND11_MODULE(_core, m) {
             })
         .def("reshape", [](const Tensor& t, const py::object& s) { return t.reshape(to_shape(s)); })
         .def("unsqueeze", &Tensor::unsqueeze)
-        .def("squeeze", &Tensor::squeeze);
+        .def("squeeze", &Tensor::squeeze)
+        .def("slice", &Tensor::slice, "slice(dim, start, end): a view (napi slice, tensor.cpp:243-258)");
 
     py::class_<GradTensor, GradPtr>(m, "GradTensor")
         .def(py::init([](const Tensor& t, bool rg) { return GradTensor::make(t, rg); }), py::arg("tensor"),

@@ -228,6 +228,20 @@ Tensor Tensor::reshape(const Shape& s) const {
     return is_contiguous() ? view(res) : contiguous().view(res);
 }
 
+// tensor.cpp:243-258: a view sharing the storage; negative bounds count from
+// the end, `end` is clamped to the extent, and an empty range is an error.
+Tensor Tensor::slice(int dim, int64_t start, int64_t end) const {
+    dim = norm_axis(dim, ndim());
+    if (start < 0) start += shape_[dim];
+    if (end < 0) end += shape_[dim];
+    if (end > shape_[dim]) end = shape_[dim];
+    if (start < 0 || start >= end) throw std::runtime_error("slice: start >= end");
+    Tensor r = *this;
+    r.offset_ += start * strides_[dim];
+    r.shape_[dim] = end - start;
+    return r;
+}
+
 Tensor Tensor::squeeze(int axis) const {
     axis = norm_axis(axis, ndim());
     if (shape_[axis] != 1) throw std::runtime_error("Can only squeeze size-1");

@@ -57,6 +57,7 @@ class Tensor {
     Tensor transpose(int d0, int d1) const;
     Tensor view(const Shape& s) const;
     Tensor reshape(const Shape& s) const;
+    Tensor slice(int dim, int64_t start, int64_t end) const;  // tensor.cpp:243-258
     Tensor squeeze(int axis) const;
     Tensor unsqueeze(int axis) const;
 
