@@ -43,30 +43,50 @@ namespace jst {
 namespace tc {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 16;  // fp32 elements per k-slab: 64-byte rows, swizzle-64B
-constexpr int STAGES = 4;
 constexpr int THREADS = 192;
-// Two fp32 accumulators of 128 lanes x 256 columns: D_hi receives only the
-// A_hi*B_hi products, D_lo the two small cross products.  The tensor core's
-// fp32 accumulation truncates each add relative to the accumulator's own
-// magnitude, so keeping the ~2^-11 smaller cross terms out of D_hi cuts the
-// number of truncating adds into the large accumulator by three.
-constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t D_HI_COL = 0;
-constexpr uint32_t D_LO_COL = 256;
-
-constexpr uint32_t A_TILE_BYTES = BM * BK * 4;  // 8 KiB
-constexpr uint32_t B_TILE_BYTES = BN * BK * 4;  // 16 KiB
-constexpr uint32_t STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;  // 48 KiB
-constexpr uint32_t RING_BYTES = STAGES * STAGE_BYTES;                  // 192 KiB
 // Epilogue staging: each of the 4 epilogue warps transposes its 32 x 32 fp32
 // block through shared memory (rows 36 floats apart: 16-byte aligned and
 // bank-conflict free for the float4 accesses) so that every store instruction
 // writes four full 128-byte row segments of C.
 constexpr int STG_LD = 36;
 constexpr uint32_t STG_BYTES = 4 * 32 * STG_LD * 4;  // 18 KiB
-constexpr uint32_t SMEM_BYTES = RING_BYTES + 1024 /*align slack*/ + 256 /*barriers*/ + STG_BYTES;
+
+// Tile configurations: BN columns of C per CTA, STAGES-deep TMA ring.
+// Two fp32 accumulators of 128 lanes x BN columns: D_hi receives only the
+// A_hi*B_hi products, D_lo the two small cross products.  The tensor core's
+// fp32 accumulation truncates each add relative to the accumulator's own
+// magnitude, so keeping the ~2^-11 smaller cross terms out of D_hi cuts the
+// number of truncating adds into the large accumulator by three.
+//   BN = 256, 4 stages: 512 TMEM columns, 193 KiB of shared memory, one CTA
+//     per SM -- the large-GEMM configuration;
+//   BN = 128, 3 stages and BN = 64, 4 stages: 256 / 128 TMEM columns and
+//     97 KiB, so two CTAs share an SM and one's epilogue overlaps the other's
+//     main loop -- for narrow outputs (N <= 128) and short K, where a lone CTA
+//     spends most of its time outside the MMA loop or waiting on memory.
+template <int BN_, int STAGES_>
+struct Cfg {
+    static constexpr int BN = BN_;
+    static constexpr int STAGES = STAGES_;
+    static constexpr uint32_t TMEM_COLS = BN_ == 256 ? 512 : (BN_ == 128 ? 256 : 128);
+    static constexpr uint32_t D_HI_COL = 0;
+    static constexpr uint32_t D_LO_COL = BN_;
+    static constexpr uint32_t A_TILE_BYTES = BM * BK * 4;
+    static constexpr uint32_t B_TILE_BYTES = BN_ * BK * 4;
+    static constexpr uint32_t STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;
+    static constexpr uint32_t RING_BYTES = STAGES_ * STAGE_BYTES;
+    // The epilogue's staging tiles reuse the start of the ring: by the time the
+    // accumulator is complete every TMA write and tensor-core read of the ring
+    // has finished.
+    static_assert(RING_BYTES >= STG_BYTES, "staging aliases the ring");
+    static constexpr uint32_t SMEM_BYTES = RING_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+    static constexpr int MIN_BLOCKS = SMEM_BYTES <= 113 * 1024 ? 2 : 1;
+    static_assert(2 * BN_ <= (int)TMEM_COLS, "accumulators must fit the TMEM allocation");
+    static_assert(STAGES_ * 3 + 1 <= 30, "barrier area");
+};
+using CfgWide = Cfg<256, 4>;
+using CfgMid = Cfg<128, 3>;
+using CfgNarrow = Cfg<64, 4>;
 
 struct Params {
     int M, N, K, batch;
@@ -83,6 +103,7 @@ struct Params {
     int a_bcast, b_bcast;  // operand planes hold one batch entry shared by every batch
     int kslices;           // > 1: split K; C receives partials [slice][batch][M][N]
     int kb_per_slice;      // BK steps per slice
+    int split_a;           // tm_a_hi maps the raw fp32 A; the epilogue warps split it in shared memory
 };
 
 __device__ __forceinline__ float epi(float v, const float* bias, int col, int relu) {
@@ -91,16 +112,23 @@ __device__ __forceinline__ float epi(float v, const float* bias, int col, int re
     return v;
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+template <class C>
+__global__ void __launch_bounds__(THREADS, C::MIN_BLOCKS)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
                    const __grid_constant__ CUtensorMap tm_b_hi, const __grid_constant__ CUtensorMap tm_b_lo,
                    const Params p) {
+    constexpr int BN = C::BN;
+    constexpr int STAGES = C::STAGES;
+    constexpr uint32_t TMEM_COLS = C::TMEM_COLS, D_HI_COL = C::D_HI_COL, D_LO_COL = C::D_LO_COL;
+    constexpr uint32_t A_TILE_BYTES = C::A_TILE_BYTES, B_TILE_BYTES = C::B_TILE_BYTES;
+    constexpr uint32_t STAGE_BYTES = C::STAGE_BYTES, RING_BYTES = C::RING_BYTES;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment keeps every tile on a swizzle-pattern boundary
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + RING_BYTES);
     uint64_t* empty_bar = full_bar + STAGES;
-    uint64_t* accum_bar = empty_bar + STAGES;
+    uint64_t* conv_bar = empty_bar + STAGES;  // split_a: the stage's A tile has been split
+    uint64_t* accum_bar = conv_bar + STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
     volatile uint32_t* err = tmem_slot + 1;
 
@@ -133,6 +161,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int s = 0; s < STAGES; ++s) {
             ptx::mbar_init(&full_bar[s], 1);
             ptx::mbar_init(&empty_bar[s], 1);
+            ptx::mbar_init(&conv_bar[s], 4);  // one arrival per splitting warp
         }
         ptx::mbar_init(accum_bar, 1);
         *err = 0;
@@ -156,10 +185,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t phase = (kb / STAGES) & 1;
                 if (!ptx::mbar_wait(&empty_bar[s], phase ^ 1, err)) break;
                 uint8_t* st = smem + s * STAGE_BYTES;
-                ptx::mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+                ptx::mbar_arrive_expect_tx(&full_bar[s], p.split_a ? STAGE_BYTES - A_TILE_BYTES : STAGE_BYTES);
                 const int kx = (kb0 + kb) * BK;
-                ptx::tma_load_3d(st, &tm_a_hi, &full_bar[s], kx, m0, za);
-                ptx::tma_load_3d(st + A_TILE_BYTES, &tm_a_lo, &full_bar[s], kx, m0, za);
+                ptx::tma_load_3d(st, &tm_a_hi, &full_bar[s], kx, m0, za);  // split_a: the raw fp32 tile
+                if (!p.split_a) ptx::tma_load_3d(st + A_TILE_BYTES, &tm_a_lo, &full_bar[s], kx, m0, za);
                 ptx::tma_load_3d(st + 2 * A_TILE_BYTES, &tm_b_hi, &full_bar[s], kx, n0, zb);
                 ptx::tma_load_3d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_b_lo, &full_bar[s], kx, n0, zb);
             }
@@ -172,7 +201,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int kb = 0; kb < num_kb && ok; ++kb) {
                 const int s = kb % STAGES;
                 const uint32_t phase = (kb / STAGES) & 1;
-                if (!ptx::mbar_wait(&full_bar[s], phase, err)) { ok = false; break; }
+                if (!ptx::mbar_wait(p.split_a ? &conv_bar[s] : &full_bar[s], phase, err)) { ok = false; break; }
                 ptx::tc_fence_after();
                 const uint32_t st = ptx::smem_u32(smem + s * STAGE_BYTES);
                 const uint32_t a_hi = st, a_lo = st + A_TILE_BYTES;
@@ -192,6 +221,39 @@ __global__ void __launch_bounds__(THREADS, 1)
             ptx::mma_commit(accum_bar);  // always signalled, also on the error path
         }
     } else {
+        // ---------------------------------------------------- A split (split_a)
+        // The TMA wrote the raw fp32 A tile into the A_hi slot with the same
+        // swizzled placement the hi / lo planes would have, so the split is
+        // elementwise at unchanged offsets: hi in place, lo into the A_lo
+        // slot.  fence.proxy.async makes these generic stores visible to the
+        // tensor core before the warp's arrival releases the MMA issuer.
+        if (p.split_a) {
+            const int ct = threadIdx.x - 64;  // 0..127
+            for (int kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t phase = (kb / STAGES) & 1;
+                int okw = 0;
+                if (lane == 0) okw = ptx::mbar_wait(&full_bar[s], phase, err);
+                if (!__shfl_sync(0xffffffffu, okw, 0)) break;
+                float4* hi = reinterpret_cast<float4*>(smem + s * STAGE_BYTES);
+                float4* lo = reinterpret_cast<float4*>(smem + s * STAGE_BYTES + A_TILE_BYTES);
+#pragma unroll
+                for (int i = 0; i < (int)(A_TILE_BYTES / 16) / 128; ++i) {
+                    const int idx = ct + i * 128;
+                    const float4 v = hi[idx];
+                    float4 h, l;
+                    h.x = ptx::to_tf32(v.x); l.x = ptx::to_tf32(v.x - h.x);
+                    h.y = ptx::to_tf32(v.y); l.y = ptx::to_tf32(v.y - h.y);
+                    h.z = ptx::to_tf32(v.z); l.z = ptx::to_tf32(v.z - h.z);
+                    h.w = ptx::to_tf32(v.w); l.w = ptx::to_tf32(v.w - h.w);
+                    hi[idx] = h;
+                    lo[idx] = l;
+                }
+                ptx::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&conv_bar[s]);
+            }
+        }
         // ---------------------------------------------------- epilogue
         // one lane waits and broadcasts, so the warp stays converged for the
         // .sync.aligned TMEM loads below
@@ -206,7 +268,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         float* crow = cbase + (int64_t)row * p.ldc;
         const bool vec = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                          ((p.strideC & 3) == 0);
-        float* stg = reinterpret_cast<float*>(smem + RING_BYTES + 256) + (warp - 2) * (32 * STG_LD);
+        float* stg = reinterpret_cast<float*>(smem) + (warp - 2) * (32 * STG_LD);  // aliases ring stage 0
         // a row bias is added in registers before epi(); epi() then sees no column bias
         const bool row_bias = p.bias_row && p.bias;
         const float* cbias = p.bias_row ? nullptr : p.bias;
@@ -377,6 +439,24 @@ static bool make_plane_map(CUtensorMap* m, const float* base, int K, int rows, i
     return r == CUDA_SUCCESS;
 }
 
+// 3-D map over a raw K-major fp32 operand [batch][rows][K] (row stride ld,
+// batch stride bstride, elements): the tensor-core kernel splits its tiles in
+// shared memory.  Same box and swizzle as the planes.
+static bool make_raw_map(CUtensorMap* m, const float* base, int K, int rows, int batch, int64_t ld, int64_t bstride,
+                         int box_rows) {
+    auto enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
+    const int64_t bs = batch > 1 ? bstride : ld * rows;
+    cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bs * 4};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 static int launch_split(const float* src, bool kmajor, int64_t ld, int64_t sstride, int rows, int K, int Kp,
                         int batch, float* hi, float* lo, cudaStream_t s) {
     if (rows == 0 || Kp == 0) return JST_OK;
@@ -401,15 +481,27 @@ static int launch_split(const float* src, bool kmajor, int64_t ld, int64_t sstri
 
 }  // namespace tc
 
-// Split K when the output tiles fill less than one wave of 148 CTAs (one CTA
-// per SM): as many slices as still fit in the wave, each at least 64 BK steps
-// (K = 1024) long, at most 16.  The count is normalised so that no slice is
-// empty.
+// Tile configuration of a GEMM: narrow tiles for narrow outputs, and for short
+// K (the output then dominates and two co-resident CTAs overlap one's
+// epilogue with the other's main loop); the 256-wide tile otherwise.
+int tc_pick_bn(int M, int N, int K) {
+    (void)M;
+    if (N <= 64) return 64;
+    if (N <= 128 || K <= 256) return 128;
+    return 256;
+}
+
+// Split K when the output tiles fill less than half a wave (148 one-CTA or
+// 296 two-CTA slots): as many slices as still fit in the wave, each at least
+// 64 BK steps (K = 1024) long, at most 16.  The count is normalised so that
+// no slice is empty.
 int tc_split_k(const GemmArgs& a) {
-    const int64_t tiles = (int64_t)((a.M + tc::BM - 1) / tc::BM) * ((a.N + tc::BN - 1) / tc::BN) * a.batch;
+    const int bn = tc_pick_bn(a.M, a.N, a.K);
+    const int64_t slots = bn == 256 ? 148 : 296;
+    const int64_t tiles = (int64_t)((a.M + tc::BM - 1) / tc::BM) * ((a.N + bn - 1) / bn) * a.batch;
     const int num_kb = (a.K + tc::BK - 1) / tc::BK;
-    if (tiles <= 0 || tiles >= 148 / 2) return 1;
-    int S = (int)std::min<int64_t>(std::min<int64_t>(148 / tiles, num_kb / 64), 16);
+    if (tiles <= 0 || tiles >= slots / 2) return 1;
+    int S = (int)std::min<int64_t>(std::min<int64_t>(slots / tiles, num_kb / 64), 16);
     if (S <= 1) return 1;
     const int per = (num_kb + S - 1) / S;
     return (num_kb + per - 1) / per;
@@ -420,9 +512,22 @@ int tc_split_k(const GemmArgs& a) {
 static bool a_broadcast(const GemmArgs& a) { return a.batch > 1 && a.strideA == 0; }
 static bool b_broadcast(const GemmArgs& a) { return a.batch > 1 && a.strideB == 0; }
 
+// Split A inside the kernel (no A planes) when the tile is narrow -- the GEMM
+// then streams A once from memory instead of reading it, writing two planes
+// and reading those back -- and A is K-major with TMA-compatible strides.
+// The 256-wide configuration keeps the split pass: there the MMA loop is
+// already bounded by shared-memory bandwidth.
+static bool use_split_a(const GemmArgs& a) {
+    if (a.transA || tc_pick_bn(a.M, a.N, a.K) == 256) return false;
+    if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (a.lda & 3)) return false;
+    if (a.batch > 1 && !a_broadcast(a) && (a.strideA & 3)) return false;
+    return true;
+}
+
 size_t tc_workspace_bytes(const GemmArgs& a) {
     const size_t Kp = (size_t)((a.K + 3) & ~3);
-    const size_t ab = a_broadcast(a) ? 1 : (size_t)a.batch, bb = b_broadcast(a) ? 1 : (size_t)a.batch;
+    const size_t ab = use_split_a(a) ? 0 : (a_broadcast(a) ? 1 : (size_t)a.batch);
+    const size_t bb = b_broadcast(a) ? 1 : (size_t)a.batch;
     const int S = tc_split_k(a);
     const size_t part = S > 1 ? (size_t)S * a.batch * a.M * a.N : 0;
     return (2 * Kp * ((size_t)a.M * ab + (size_t)a.N * bb) + part) * sizeof(float);
@@ -434,10 +539,35 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
     return rc ? set_status(rc, "split pass failed to launch") : JST_OK;
 }
 
+// Launch one configuration; its shared-memory opt-in is set once per device.
+template <class Cf>
+static int launch_cfg(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
+                      const CUtensorMap& b_lo, const tc::Params& p, unsigned grid, cudaStream_t s) {
+    static bool attr_set[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+            if (cudaFuncSetAttribute(tc::tc_gemm_kernel<Cf>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cf::SMEM_BYTES) != cudaSuccess)
+                return set_status(JST_ERR_CUDA, "cudaFuncSetAttribute(tc_gemm_kernel) failed");
+            attr_set[dev] = true;
+        }
+    }
+    {
+        ProfScope prof(s, KID_TC_GEMM);
+        tc::tc_gemm_kernel<Cf><<<grid, tc::THREADS, Cf::SMEM_BYTES, s>>>(a_hi, a_lo, b_hi, b_lo, p);
+    }
+    if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "tc_gemm_kernel launch failed");
+    return JST_OK;
+}
+
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
                    cudaStream_t s, int mc_store, const float* aux, int64_t ld_aux, int64_t stride_aux, int bias_row,
-                   int a_bcast, int b_bcast, int kslices) {
+                   int a_bcast, int b_bcast, int kslices, int split_a, int64_t lda_raw, int64_t strideA_raw) {
     using namespace tc;
     const int Kp = (K + 3) & ~3;
     const int num_kb = (K + BK - 1) / BK;
@@ -446,26 +576,21 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
     if ((num_kb + kb_per_slice - 1) / kb_per_slice != kslices)  // a slice would be empty
         return set_status(JST_ERR_ARG, "tc: split-K slice count leaves a slice empty");
     const int ab = a_bcast ? 1 : batch, bb = b_bcast ? 1 : batch;
+    const int bn = tc_pick_bn(M, N, K);
+    if (split_a && bn == 256) return set_status(JST_ERR_ARG, "tc: in-kernel A split needs a narrow tile");
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-    if (!make_plane_map(&m_ahi, a_hi, K, M, ab, Kp, BM) || !make_plane_map(&m_alo, a_lo, K, M, ab, Kp, BM) ||
-        !make_plane_map(&m_bhi, b_hi, K, N, bb, Kp, BN) || !make_plane_map(&m_blo, b_lo, K, N, bb, Kp, BN))
+    const bool a_ok = split_a ? make_raw_map(&m_ahi, a_hi, K, M, ab, lda_raw, strideA_raw, BM)
+                              : (make_plane_map(&m_ahi, a_hi, K, M, ab, Kp, BM) &&
+                                 make_plane_map(&m_alo, a_lo, K, M, ab, Kp, BM));
+    if (split_a) m_alo = m_ahi;  // not read
+    if (!a_ok || !make_plane_map(&m_bhi, b_hi, K, N, bb, Kp, bn) || !make_plane_map(&m_blo, b_lo, K, N, bb, Kp, bn))
         return set_status(JST_ERR_CUDA, "cuTensorMapEncodeTiled failed");
-
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
-            cudaSuccess)
-            return set_status(JST_ERR_CUDA, "cudaFuncSetAttribute(tc_gemm_kernel) failed");
-        attr_set[dev] = true;
-    }
     Params p;
     p.M = M; p.N = N; p.K = K; p.batch = batch;
     p.C = C; p.ldc = ldc; p.strideC = strideC;
     p.bias = bias; p.bias_row = bias_row; p.relu = relu;
     p.tiles_m = (M + BM - 1) / BM;
-    p.tiles_n = (N + BN - 1) / BN;
+    p.tiles_n = (N + bn - 1) / bn;
     p.err = err;
     p.mc_store = mc_store;
     p.aux = aux;
@@ -475,14 +600,14 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
     p.b_bcast = b_bcast;
     p.kslices = kslices;
     p.kb_per_slice = kb_per_slice;
+    p.split_a = split_a;
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * batch * kslices;
     if (grid > 0x7fffffff) return set_status(JST_ERR_ARG, "tc: too many tiles");
-    {
-        ProfScope prof(s, KID_TC_GEMM);
-        tc_gemm_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, s>>>(m_ahi, m_alo, m_bhi, m_blo, p);
-    }
-    if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "tc_gemm_kernel launch failed");
-    return JST_OK;
+    int rc;
+    if (bn == 256) rc = launch_cfg<CfgWide>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s);
+    else if (bn == 128) rc = launch_cfg<CfgMid>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s);
+    else rc = launch_cfg<CfgNarrow>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s);
+    return rc;
 }
 
 // Split both operands into `workspace` and run the tensor-core kernel;
@@ -490,9 +615,9 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
 static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cudaStream_t s) {
     const int Kp = (a.K + 3) & ~3;
     float* ws = static_cast<float*>(workspace);
-    const bool abc = a_broadcast(a), bbc = b_broadcast(a);
+    const bool abc = a_broadcast(a), bbc = b_broadcast(a), sa = use_split_a(a);
     const int ab = abc ? 1 : a.batch, bb = bbc ? 1 : a.batch;
-    const size_t a_plane = (size_t)ab * a.M * Kp;
+    const size_t a_plane = sa ? 0 : (size_t)ab * a.M * Kp;
     const size_t b_plane = (size_t)bb * a.N * Kp;
     float* a_hi = ws;
     float* a_lo = a_hi + a_plane;
@@ -500,17 +625,18 @@ static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cud
     float* b_lo = b_hi + b_plane;
     float* part = b_lo + b_plane;
     // op(A) rows are M: K-major unless A is stored transposed.
-    int rc = tc_split(a.A, !a.transA, a.lda, a.strideA, a.M, a.K, ab, a_hi, a_lo, s);
+    int rc = sa ? JST_OK : tc_split(a.A, !a.transA, a.lda, a.strideA, a.M, a.K, ab, a_hi, a_lo, s);
     if (rc) return rc;
+    const float* ah = sa ? a.A : a_hi;
     // op(B)^T rows are N: K-major when B is stored [N, K] (transB).
     rc = tc_split(a.B, a.transB, a.ldb, a.strideB, a.N, a.K, bb, b_hi, b_lo, s);
     if (rc) return rc;
     const int S = tc_split_k(a);
     if (S <= 1)
-        return tc_gemm_planes(a_hi, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, a.C, a.ldc, a.strideC, a.bias, a.relu,
-                              err, s, 0, a.aux, a.ld_aux, a.stride_aux, a.bias_row, abc, bbc, 1);
-    rc = tc_gemm_planes(a_hi, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, part, a.N, (int64_t)a.M * a.N, nullptr, 0, err,
-                        s, 0, nullptr, 0, 0, 0, abc, bbc, S);
+        return tc_gemm_planes(ah, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, a.C, a.ldc, a.strideC, a.bias, a.relu, err,
+                              s, 0, a.aux, a.ld_aux, a.stride_aux, a.bias_row, abc, bbc, 1, sa, a.lda, a.strideA);
+    rc = tc_gemm_planes(ah, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, part, a.N, (int64_t)a.M * a.N, nullptr, 0, err,
+                        s, 0, nullptr, 0, 0, 0, abc, bbc, S, sa, a.lda, a.strideA);
     if (rc) return rc;
     return splitk_reduce_run(splitk_reduce_args(a, part, S), s);
 }
