@@ -13,7 +13,12 @@
 //     one fused gate kernel that reads gi, gh and h and writes h' straight
 //     into the output sequence, which is also the next step's h;
 //   * at the first step with no initial state, gh = b_hh and the GEMM is
-//     skipped.
+//     skipped;
+//   * for realistic sizes the recurrent product runs on the tensor cores as
+//     ghT = W_hh . h^T: W_hh is split into tf32 planes once per call, each
+//     step splits only h, the GEMM is cut into K-slices so its few output
+//     tiles fill the SMs, and one kernel sums the slices in order, adds b_hh
+//     and applies the gates.
 // The gate arithmetic follows the reference op by op in fp32: sigmoid as
 // 1 / (1 + __expf(-x)) and tanhf (native/ops/kernels.cuh:48-49), (1 - z) as
 // (-z) + 1, and h' = ((1 - z) * n) + (z * h) with each product rounded.
@@ -59,6 +64,39 @@ __global__ void gru_gate_kernel(const float* __restrict__ gi, const float* __res
     }
 }
 
+// Tensor-core step: ghT partials part[s][3H][batch] (K-slices of W_hh . h^T);
+// sums the slices in order, adds b_hh and applies the gates (same arithmetic
+// as gru_gate_kernel).  One thread per (b, j), j fastest... the partials are
+// [row][batch], so consecutive threads take consecutive b for coalescing.
+__global__ void gru_gate_t_kernel(const float* __restrict__ gi, const float* __restrict__ part, int slices,
+                                  const float* __restrict__ b_hh, const float* __restrict__ h_prev, int64_t ld_prev,
+                                  float* __restrict__ h_out, int64_t ld_out, int batch, int H) {
+    const int64_t total = (int64_t)batch * H;
+    const int64_t plane = 3LL * H * batch;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int j = (int)(i / batch), b = (int)(i - (int64_t)j * batch);
+        float ghr = 0.0f, ghz = 0.0f, ghn = 0.0f;
+        for (int s = 0; s < slices; ++s) {
+            const float* ps = part + s * plane;
+            ghr += ps[(int64_t)j * batch + b];
+            ghz += ps[(int64_t)(H + j) * batch + b];
+            ghn += ps[(int64_t)(2 * H + j) * batch + b];
+        }
+        if (b_hh) {
+            ghr = __fadd_rn(ghr, b_hh[j]);
+            ghz = __fadd_rn(ghz, b_hh[H + j]);
+            ghn = __fadd_rn(ghn, b_hh[2 * H + j]);
+        }
+        const float* gib = gi + (int64_t)b * 3 * H;
+        const float r = sigmoid_ref(__fadd_rn(gib[j], ghr));
+        const float z = sigmoid_ref(__fadd_rn(gib[H + j], ghz));
+        const float n = tanhf(__fadd_rn(gib[2 * H + j], __fmul_rn(r, ghn)));
+        const float h = h_prev[(int64_t)b * ld_prev + j];
+        const float one_minus_z = __fadd_rn(-z, 1.0f);
+        h_out[(int64_t)b * ld_out + j] = __fadd_rn(__fmul_rn(one_minus_z, n), __fmul_rn(z, h));
+    }
+}
+
 int gate(const float* gi, const float* gh, const float* b_hh, const float* h_prev, int64_t ld_prev, float* h_out,
          int64_t ld_out, int batch, int H, cudaStream_t s) {
     const int64_t total = (int64_t)batch * H;
@@ -82,6 +120,25 @@ int nt_gemm(const float* A, int64_t lda, const float* W, const float* bias, floa
     d.epilogue = bias ? JST_EPI_BIAS : JST_EPI_NONE;
     d.stream = reinterpret_cast<jst_stream_t>(s);
     return jst_gemm_ex(&d);
+}
+
+// Recurrent GEMM on the tensor cores: worth it once the step's product is
+// large enough to cover the split of h and the reduce.
+bool use_tc_recurrent(int batch, int H) {
+    return H >= 128 && batch >= 8 && (double)3 * H * H * batch >= (double)(1 << 24);
+}
+
+// K-slices for ghT = W_hh . h^T (M = 3H, N = batch): fill the SMs with
+// (tile, slice) CTAs, slices of at least 4 BK steps; normalised so that no
+// slice is empty.
+int recurrent_slices(int batch, int H) {
+    const int bn = tc_pick_bn(3 * H, batch, H);
+    const int tiles = ((3 * H + 127) / 128) * ((batch + bn - 1) / bn);
+    const int num_kb = (H + 15) / 16;
+    int S = std::min(std::min(148 / std::max(tiles, 1), num_kb / 4), 16);
+    if (S <= 1) return 1;
+    const int per = (num_kb + S - 1) / S;
+    return (num_kb + per - 1) / per;
 }
 
 }  // namespace
@@ -108,25 +165,62 @@ extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int inp
     }
     if (!x || !w_ih || !w_hh || !out) return set_status(JST_ERR_ARG, "gru: null pointer");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const bool tc = use_tc_recurrent(batch, hidden);
+    const int Kp = (hidden + 3) & ~3;
+    const int S = tc ? recurrent_slices(batch, hidden) : 1;
+    // workspace: gi [seq][batch][3H]; gh [batch][3H]; tensor-core path: W_hh
+    // planes [3H][Kp] x2, h planes [batch][Kp] x2, partials [S][3H][batch]
+    // every region starts on a 256-byte boundary (the planes are TMA sources)
+    auto up = [](size_t n) { return (n + 63) & ~size_t(63); };
+    const size_t n_gi = up((size_t)rows * G), n_gh = up((size_t)batch * G);
+    const size_t n_w = tc ? up((size_t)G * Kp) : 0, n_h = tc ? up((size_t)batch * Kp) : 0;
+    const size_t n_part = tc ? up((size_t)S * G * batch) : 0;
     void* ws = nullptr;
-    int rc = workspace_alloc((size_t)(rows + batch) * G * sizeof(float), s, &ws);
+    int rc = workspace_alloc((n_gi + n_gh + 2 * n_w + 2 * n_h + n_part) * sizeof(float), s, &ws);
     if (rc) return rc;
     float* gi = static_cast<float*>(ws);  // [seq][batch][3H]
-    float* gh = gi + rows * G;            // [batch][3H]
+    float* gh = gi + n_gi;                // [batch][3H]
+    float* w_hi = gh + n_gh;
+    float* w_lo = w_hi + n_w;
+    float* h_hi = w_lo + n_w;
+    float* h_lo = h_hi + n_h;
+    float* part = h_lo + n_h;
     // all input projections at once (nn.js:480 for every step)
     rc = nt_gemm(x, input_size, w_ih, b_ih, gi, (int)rows, (int)G, input_size, s);
+    // W_hh is the same at every step: split it once
+    if (!rc && tc) rc = tc_split(w_hh, 1, hidden, 0, (int)G, hidden, 1, w_hi, w_lo, s);
     const float* h_prev = h0;  // row stride `hidden` for h0, ld_out for rows of `out`
     int64_t ld_prev = hidden;
     for (int step = 0; step < seq && !rc; ++step) {
         const int t = reverse ? seq - 1 - step : step;
-        const float* ghp = nullptr;
-        if (h_prev) {  // nn.js:481
-            rc = nt_gemm(h_prev, ld_prev, w_hh, b_hh, gh, batch, (int)G, hidden, s);
-            if (rc) break;
-            ghp = gh;
-        }
         float* h_out = out + (int64_t)t * batch * ld_out;
-        rc = gate(gi + (int64_t)t * batch * G, ghp, b_hh, h_prev, ld_prev, h_out, ld_out, batch, hidden, s);
+        const float* git = gi + (int64_t)t * batch * G;
+        if (h_prev && tc) {
+            // nn.js:481 as ghT[3H][batch] = W_hh . h^T on the tensor cores, split over K,
+            // the slices summed with b_hh and the gates in one kernel
+            rc = tc_split(h_prev, 1, ld_prev, 0, batch, hidden, 1, h_hi, h_lo, s);
+            if (!rc)
+                rc = tc_gemm_planes(w_hi, w_lo, h_hi, h_lo, (int)G, batch, hidden, 1, part, batch, G * batch, nullptr,
+                                    0, device_error_word(), s, 0, nullptr, 0, 0, 0, 0, 0, S);
+            if (!rc) {
+                const int64_t total = (int64_t)batch * hidden;
+                const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
+                {
+                    ProfScope prof(s, KID_RNN);
+                    gru_gate_t_kernel<<<blocks, 256, 0, s>>>(git, part, S, b_hh, h_prev, ld_prev, h_out, ld_out,
+                                                             batch, hidden);
+                }
+                if (cudaPeekAtLastError() != cudaSuccess) rc = set_status(JST_ERR_CUDA, "gru gate launch failed");
+            }
+        } else {
+            const float* ghp = nullptr;
+            if (h_prev) {  // nn.js:481
+                rc = nt_gemm(h_prev, ld_prev, w_hh, b_hh, gh, batch, (int)G, hidden, s);
+                if (rc) break;
+                ghp = gh;
+            }
+            rc = gate(git, ghp, b_hh, h_prev, ld_prev, h_out, ld_out, batch, hidden, s);
+        }
         h_prev = h_out;
         ld_prev = ld_out;
     }

@@ -40,7 +40,8 @@ def _run(seq, batch, inp, H, layers, bidir, with_h0, batch_first=False, seed=0):
 @pytest.mark.parametrize("seq,batch,inp,H,layers,bidir,with_h0", [
     (5, 3, 7, 9, 1, False, False),       # odd sizes, zero initial state
     (12, 16, 64, 128, 2, True, True),    # stacked, bidirectional, given h0
-    (40, 64, 256, 512, 1, False, True),  # recurrent GEMMs of a realistic size
+    (40, 64, 256, 512, 1, False, True),  # recurrent GEMMs of a realistic size (tensor-core step)
+    (10, 24, 96, 512, 2, True, True),    # tensor-core step, bidirectional, batch not a multiple of 4
     (3, 1, 1, 1, 1, True, False),        # the degenerate one-unit case
 ])
 def test_gru_against_oracle(seq, batch, inp, H, layers, bidir, with_h0):
