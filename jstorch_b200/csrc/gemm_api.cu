@@ -208,12 +208,16 @@ struct HostStage {
 };
 static HostStage g_host[64];
 
-// Pipelined host GEMM for large tensor-core shapes: A is moved and multiplied
-// in row chunks so that its host->device copies (copy stream h2d), the split +
-// GEMM of the previous chunk (compute stream st) and the device->host copy of
-// C chunks (copy stream d2h) overlap.  B is copied and split once first.
+// Large host-array products: C is cut into a grid of blocks (about 4 x 4,
+// at least 1024 x 1024), A into the matching row blocks and B into column
+// panels.  The host->device copies alternate between A blocks and B panels
+// (proportionally), each block's GEMM starts as soon as its row block and its
+// panel are on the device, and each C block goes back to the host as soon as
+// it is done -- so compute starts after about a quarter of each operand has
+// arrived and the device->host traffic runs under the host->device traffic
+// instead of after it.  B panels and C blocks move as pitched 2-D copies.
 // All three streams are ordered after the caller's earlier work on st, and st
-// is ordered after the last C chunk has reached the host buffer.
+// is ordered after the last C block has reached the host buffer.
 static int host_matmul_pipelined(HostStage& h, const float* a, const float* b, float* c, int M, int K, int N,
                                  float* dA, float* dB, float* dC, cudaStream_t st) {
     int rc;
@@ -224,19 +228,25 @@ static int host_matmul_pipelined(HostStage& h, const float* a, const float* b, f
         if (rc) return rc;
     }
     const int64_t Kp = (K + 3) & ~3;
-    int64_t R = ((int64_t)M + 7) / 8;
-    R = std::max<int64_t>(1024, (R + 127) / 128 * 128);
-    const int nchunks = (int)((M + R - 1) / R);
-    const size_t nev = 3 + 2 * (size_t)nchunks;
+    auto split_dim = [](int n, int align) {
+        int64_t blk = std::max<int64_t>(1024, ((int64_t)(n + 3) / 4 + align - 1) / align * align);
+        std::vector<std::pair<int, int>> v;  // (start, extent)
+        for (int64_t x = 0; x < n; x += blk) v.push_back({(int)x, (int)std::min<int64_t>(blk, n - x)});
+        return v;
+    };
+    const auto rb = split_dim(M, 128), cb = split_dim(N, 256);
+    const int gr = (int)rb.size(), gc = (int)cb.size();
+    const size_t nev = 3 + (size_t)gr + gc + (size_t)gr * gc;
     while (h.ev.size() < nev) {
         cudaEvent_t e;
         rc = cuda_status(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event create");
         if (rc) return rc;
         h.ev.push_back(e);
     }
-    cudaEvent_t ev_entry = h.ev[0], ev_b = h.ev[1], ev_done = h.ev[2];
-    auto ev_a = [&](int i) { return h.ev[3 + 2 * i]; };
-    auto ev_c = [&](int i) { return h.ev[4 + 2 * i]; };
+    cudaEvent_t ev_entry = h.ev[0], ev_done = h.ev[2];
+    auto ev_a = [&](int i) { return h.ev[3 + i]; };
+    auto ev_b = [&](int j) { return h.ev[3 + gr + j]; };
+    auto ev_c = [&](int i, int j) { return h.ev[3 + gr + gc + (size_t)i * gc + j]; };
     const size_t a_plane = (size_t)M * Kp, b_plane = (size_t)N * Kp;
     void* ws = nullptr;
     rc = workspace_alloc((2 * a_plane + 2 * b_plane) * sizeof(float), st, &ws);
@@ -246,37 +256,64 @@ static int host_matmul_pipelined(HostStage& h, const float* a, const float* b, f
     float* b_hi = a_lo + a_plane;
     float* b_lo = b_hi + b_plane;
     uint32_t* err = device_error_word();
+    const size_t pitch = (size_t)N * sizeof(float);
 
     rc = cuda_status(cudaEventRecord(ev_entry, st), "event record");
     if (!rc) rc = cuda_status(cudaStreamWaitEvent(h.h2d, ev_entry, 0), "stream wait");
     if (!rc) rc = cuda_status(cudaStreamWaitEvent(h.d2h, ev_entry, 0), "stream wait");
-    if (!rc) rc = cuda_status(cudaMemcpyAsync(dB, b, (size_t)K * N * sizeof(float), cudaMemcpyHostToDevice, h.h2d),
-                              "H2D B");
-    if (!rc) rc = cuda_status(cudaEventRecord(ev_b, h.h2d), "event record");
-    if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, ev_b, 0), "stream wait");
-    if (!rc) rc = tc_split(dB, 0, N, 0, N, K, 1, b_hi, b_lo, st);
+    // enqueue order of the host->device copies (A block i or B panel j), proportional
+    std::vector<std::pair<char, int>> loads;
+    for (int ia = 0, ib = 0; ia < gr || ib < gc;) {
+        if (ib >= gc || (ia < gr && (int64_t)ia * gc <= (int64_t)ib * gr)) loads.push_back({'A', ia++});
+        else loads.push_back({'B', ib++});
+    }
     // inputs and compute first: with pageable host memory each H2D copy blocks
     // the host, and the C copies must not be queued ahead of them
-    for (int i = 0; i < nchunks && !rc; ++i) {
-        const int64_t r0 = (int64_t)i * R;
-        const int rows = (int)std::min<int64_t>(R, M - r0);
-        rc = cuda_status(cudaMemcpyAsync(dA + r0 * K, a + r0 * K, (size_t)rows * K * sizeof(float),
-                                         cudaMemcpyHostToDevice, h.h2d), "H2D A chunk");
-        if (!rc) rc = cuda_status(cudaEventRecord(ev_a(i), h.h2d), "event record");
-        if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, ev_a(i), 0), "stream wait");
-        if (!rc) rc = tc_split(dA + r0 * K, 1, K, 0, rows, K, 1, a_hi + r0 * Kp, a_lo + r0 * Kp, st);
-        if (!rc)
-            rc = tc_gemm_planes(a_hi + r0 * Kp, a_lo + r0 * Kp, b_hi, b_lo, rows, N, K, 1, dC + r0 * N, N, 0, nullptr,
-                                0, err, st);
-        if (!rc) rc = cuda_status(cudaEventRecord(ev_c(i), st), "event record");
+    std::vector<std::pair<int, int>> order;  // blocks that just became computable
+    std::vector<std::pair<int, int>> done;   // blocks in compute order
+    int na = 0, nb = 0;
+    for (size_t l = 0; l < loads.size() && !rc; ++l) {
+        if (loads[l].first == 'A') {
+            const int i = loads[l].second;
+            const int r0 = rb[i].first, rows = rb[i].second;
+            rc = cuda_status(cudaMemcpyAsync(dA + (int64_t)r0 * K, a + (int64_t)r0 * K, (size_t)rows * K * sizeof(float),
+                                             cudaMemcpyHostToDevice, h.h2d), "H2D A block");
+            if (!rc) rc = cuda_status(cudaEventRecord(ev_a(i), h.h2d), "event record");
+            if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, ev_a(i), 0), "stream wait");
+            if (!rc) rc = tc_split(dA + (int64_t)r0 * K, 1, K, 0, rows, K, 1, a_hi + r0 * Kp, a_lo + r0 * Kp, st);
+            ++na;
+            for (int j = 0; j < nb && !rc; ++j) order.push_back({i, j});
+        } else {
+            const int j = loads[l].second;
+            const int c0 = cb[j].first, cols = cb[j].second;
+            rc = cuda_status(cudaMemcpy2DAsync(dB + c0, pitch, b + c0, pitch, (size_t)cols * sizeof(float), K,
+                                               cudaMemcpyHostToDevice, h.h2d), "H2D B panel");
+            if (!rc) rc = cuda_status(cudaEventRecord(ev_b(j), h.h2d), "event record");
+            if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, ev_b(j), 0), "stream wait");
+            if (!rc) rc = tc_split(dB + c0, 0, N, 0, cols, K, 1, b_hi + c0 * Kp, b_lo + c0 * Kp, st);
+            ++nb;
+            for (int i = 0; i < na && !rc; ++i) order.push_back({i, j});
+        }
+        // the blocks that just became computable
+        while (!rc && !order.empty()) {
+            const int i = order.front().first, j = order.front().second;
+            order.erase(order.begin());
+            const int r0 = rb[i].first, rows = rb[i].second, c0 = cb[j].first, cols = cb[j].second;
+            rc = tc_gemm_planes(a_hi + r0 * Kp, a_lo + r0 * Kp, b_hi + c0 * Kp, b_lo + c0 * Kp, rows, cols, K, 1,
+                                dC + (int64_t)r0 * N + c0, N, 0, nullptr, 0, err, st);
+            if (!rc) rc = cuda_status(cudaEventRecord(ev_c(i, j), st), "event record");
+            if (rc) break;
+            done.push_back({i, j});
+        }
     }
-    for (int i = 0; i < nchunks && !rc; ++i) {
-        const int64_t r0 = (int64_t)i * R;
-        const int rows = (int)std::min<int64_t>(R, M - r0);
-        rc = cuda_status(cudaStreamWaitEvent(h.d2h, ev_c(i), 0), "stream wait");
+    for (size_t q = 0; q < done.size() && !rc; ++q) {
+        const int i = done[q].first, j = done[q].second;
+        const int r0 = rb[i].first, rows = rb[i].second, c0 = cb[j].first, cols = cb[j].second;
+        rc = cuda_status(cudaStreamWaitEvent(h.d2h, ev_c(i, j), 0), "stream wait");
         if (!rc)
-            rc = cuda_status(cudaMemcpyAsync(c + r0 * N, dC + r0 * N, (size_t)rows * N * sizeof(float),
-                                             cudaMemcpyDeviceToHost, h.d2h), "D2H C chunk");
+            rc = cuda_status(cudaMemcpy2DAsync(c + (int64_t)r0 * N + c0, pitch, dC + (int64_t)r0 * N + c0, pitch,
+                                               (size_t)cols * sizeof(float), rows, cudaMemcpyDeviceToHost, h.d2h),
+                             "D2H C block");
     }
     if (!rc) rc = cuda_status(cudaEventRecord(ev_done, h.d2h), "event record");
     if (!rc) rc = cuda_status(cudaStreamWaitEvent(st, ev_done, 0), "stream wait");

@@ -201,12 +201,14 @@ def test_kernel_choice_heuristic(jst):
 
 @pytest.mark.parametrize("pinned", [False, True])
 def test_host_matmul_pipelined_chunks(jst, pinned):
-    """Large host-array products take the chunked path (H2D / GEMM / D2H
-    overlapped on three streams); a ragged last chunk and both pageable and
+    """Large host-array products take the blocked path (H2D of A row blocks
+    and B column panels, block GEMMs, D2H of C blocks, overlapped on three
+    streams); ragged last blocks in both directions and both pageable and
     pinned host buffers must give the same product."""
     import torch
     rng = np.random.default_rng(21)
-    M, K, N = 2304, 520, 648  # chunks of 1024, 1024, 256 rows
+    M, K, N = 2500, 300, 2300  # 3 x 3 blocks: rows 1024, 1024, 452; columns 1024, 1024, 252
+    assert jst.select_kernel(M, N, K) == "tc3xtf32"  # the pipelined path is the tensor-core one
     A = rng.standard_normal((M, K), dtype=np.float32)
     B = rng.standard_normal((K, N), dtype=np.float32)
     if pinned:
@@ -218,7 +220,7 @@ def test_host_matmul_pipelined_chunks(jst, pinned):
         C = c_h.numpy()
     else:
         C = jst.torch.matmul(A, B, M, K, N).reshape(M, N)
-    rows = np.array([0, 1, 1023, 1024, 2047, 2048, 2303], np.int32)
+    rows = np.array([0, 1, 1023, 1024, 2047, 2048, 2499], np.int32)
     ref = oracle.gemm_f64(A, B, rows=rows)
     err, where = oracle.max_rel_err(A, B, C, ref, rows=rows)
     assert err <= TOL, (err, where)
