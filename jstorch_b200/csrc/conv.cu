@@ -130,7 +130,7 @@ __global__ void permute_bcn_kernel(const float* __restrict__ src, float* __restr
 constexpr int KT_PER_BLOCK = 4;
 __global__ void __launch_bounds__(256) im2col_split_t_kernel(const float* __restrict__ x, const Geo g, int c0, int Kg,
                                                              int Kp, float* __restrict__ hi, float* __restrict__ lo) {
-    __shared__ float tile[32][33];
+    __shared__ float tile[KT_PER_BLOCK][32][33];
     __shared__ int64_t k_base[32 * KT_PER_BLOCK];
     __shared__ int k_dh[32 * KT_PER_BLOCK], k_dw[32 * KT_PER_BLOCK];
     const int b = blockIdx.z;
@@ -150,33 +150,39 @@ __global__ void __launch_bounds__(256) im2col_split_t_kernel(const float* __rest
     const int ho = n / g.Wo, wo = n - ho * g.Wo;
     const int hs = ho * g.sH, ws = wo * g.sW;
     __syncthreads();
-    for (int kt = 0; kt < KT_PER_BLOCK; ++kt) {
-        const int k0 = kb0 + kt * 32;
-        if (k0 >= Kp) break;  // block-uniform
+    // every image load of the block's KT_PER_BLOCK x 32 x 32 elements is issued
+    // before the single barrier: 16 loads in flight per thread
+    float v[KT_PER_BLOCK][4];
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-            const int kl = kt * 32 + threadIdx.y + j;
+    for (int kt = 0; kt < KT_PER_BLOCK; ++kt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int kl = kt * 32 + threadIdx.y + j * 8;
             const int64_t base = k_base[kl];
             const int ih = hs + k_dh[kl], iw = ws + k_dw[kl];
-            float v = 0.0f;
-            if (base >= 0 && n < N && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W)
-                v = __ldg(xb + base + ih * g.W + iw);
-            tile[threadIdx.y + j][threadIdx.x] = v;
+            v[kt][j] = (base >= 0 && n < N && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W)
+                           ? __ldg(xb + base + ih * g.W + iw)
+                           : 0.0f;
         }
-        __syncthreads();
+#pragma unroll
+    for (int kt = 0; kt < KT_PER_BLOCK; ++kt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tile[kt][threadIdx.y + j * 8][threadIdx.x] = v[kt][j];
+    __syncthreads();
+#pragma unroll
+    for (int kt = 0; kt < KT_PER_BLOCK; ++kt) {
+        const int k = kb0 + kt * 32 + threadIdx.x;
 #pragma unroll
         for (int j = 0; j < 32; j += 8) {
             const int nn = n0 + threadIdx.y + j;
-            const int k = k0 + threadIdx.x;
             if (nn < N && k < Kp) {
-                const float v = tile[threadIdx.x][threadIdx.y + j];
-                const float h = ptx::to_tf32(v);
+                const float val = tile[kt][threadIdx.x][threadIdx.y + j];
+                const float h = ptx::to_tf32(val);
                 const int64_t o = ((int64_t)b * N + nn) * Kp + k;
                 hi[o] = h;
-                lo[o] = ptx::to_tf32(v - h);
+                lo[o] = ptx::to_tf32(val - h);
             }
         }
-        __syncthreads();  // the tile is refilled by the next k tile
     }
 }
 

@@ -35,6 +35,8 @@ namespace {
 
 __device__ __forceinline__ float sigmoid_ref(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
+constexpr int kMaxSlices = 16;  // K-slices of the recurrent GEMM (recurrent_slices caps at 16)
+
 // h_out[b][j] from gi[b][{j, H+j, 2H+j}], gh[b][...] (or b_hh when gh is
 // null) and h_prev[b][j] (or 0 when null).
 __global__ void gru_gate_kernel(const float* __restrict__ gi, const float* __restrict__ gh,
@@ -64,37 +66,56 @@ __global__ void gru_gate_kernel(const float* __restrict__ gi, const float* __res
     }
 }
 
-// Tensor-core step: ghT partials part[s][3H][batch] (K-slices of W_hh . h^T);
-// sums the slices in order, adds b_hh and applies the gates (same arithmetic
-// as gru_gate_kernel).  One thread per (b, j), j fastest... the partials are
-// [row][batch], so consecutive threads take consecutive b for coalescing.
-__global__ void gru_gate_t_kernel(const float* __restrict__ gi, const float* __restrict__ part, int slices,
-                                  const float* __restrict__ b_hh, const float* __restrict__ h_prev, int64_t ld_prev,
-                                  float* __restrict__ h_out, int64_t ld_out, int batch, int H) {
-    const int64_t total = (int64_t)batch * H;
+// Tensor-core step: ghT partials part[s][3H][batch] (K-slices of W_hh . h^T).
+// A block of 256 threads takes 8 hidden units x 32 batch rows: it sums the
+// slices in order and adds b_hh with 32 threads along the batch per hidden
+// unit (128-byte reads of the [row][batch] partials), transposes through
+// shared memory, then applies the gates with 8 threads along the hidden units
+// per batch row (whole 32-byte sectors of gi, h and h').  Same arithmetic as
+// gru_gate_kernel.
+__global__ void __launch_bounds__(256) gru_gate_t_kernel(const float* __restrict__ gi, const float* __restrict__ part,
+                                                         int slices, const float* __restrict__ b_hh,
+                                                         const float* __restrict__ h_prev, int64_t ld_prev,
+                                                         float* __restrict__ h_out, int64_t ld_out, int batch, int H) {
+    __shared__ float g[3][8][33];  // [gate][hidden unit][batch row]
+    const int j0 = blockIdx.x * 8, b0 = blockIdx.y * 32;
     const int64_t plane = 3LL * H * batch;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int j = (int)(i / batch), b = (int)(i - (int64_t)j * batch);
-        float ghr = 0.0f, ghz = 0.0f, ghn = 0.0f;
-        for (int s = 0; s < slices; ++s) {
-            const float* ps = part + s * plane;
-            ghr += ps[(int64_t)j * batch + b];
-            ghz += ps[(int64_t)(H + j) * batch + b];
-            ghn += ps[(int64_t)(2 * H + j) * batch + b];
+    const int t = threadIdx.x;
+    {
+        const int bl = t & 31, jl = t >> 5;  // sum phase: batch fastest
+        const int j = j0 + jl, b = b0 + bl;
+        float acc[3] = {0.0f, 0.0f, 0.0f};
+        if (j < H && b < batch) {
+            // all slice loads first (independent), then the sums in slice order
+            float v[3][kMaxSlices];
+#pragma unroll
+            for (int sl = 0; sl < kMaxSlices; ++sl)
+#pragma unroll
+                for (int gate = 0; gate < 3; ++gate)
+                    v[gate][sl] = sl < slices ? part[sl * plane + (int64_t)(gate * H + j) * batch + b] : 0.0f;
+#pragma unroll
+            for (int sl = 0; sl < kMaxSlices; ++sl)
+#pragma unroll
+                for (int gate = 0; gate < 3; ++gate)
+                    if (sl < slices) acc[gate] += v[gate][sl];
+            if (b_hh)
+#pragma unroll
+                for (int gate = 0; gate < 3; ++gate) acc[gate] = __fadd_rn(acc[gate], b_hh[gate * H + j]);
         }
-        if (b_hh) {
-            ghr = __fadd_rn(ghr, b_hh[j]);
-            ghz = __fadd_rn(ghz, b_hh[H + j]);
-            ghn = __fadd_rn(ghn, b_hh[2 * H + j]);
-        }
-        const float* gib = gi + (int64_t)b * 3 * H;
-        const float r = sigmoid_ref(__fadd_rn(gib[j], ghr));
-        const float z = sigmoid_ref(__fadd_rn(gib[H + j], ghz));
-        const float n = tanhf(__fadd_rn(gib[2 * H + j], __fmul_rn(r, ghn)));
-        const float h = h_prev[(int64_t)b * ld_prev + j];
-        const float one_minus_z = __fadd_rn(-z, 1.0f);
-        h_out[(int64_t)b * ld_out + j] = __fadd_rn(__fmul_rn(one_minus_z, n), __fmul_rn(z, h));
+#pragma unroll
+        for (int gate = 0; gate < 3; ++gate) g[gate][jl][bl] = acc[gate];
     }
+    __syncthreads();
+    const int jl = t & 7, bl = t >> 3;  // gate phase: hidden unit fastest
+    const int j = j0 + jl, b = b0 + bl;
+    if (b >= batch || j >= H) return;
+    const float* gib = gi + (int64_t)b * 3 * H;
+    const float r = sigmoid_ref(__fadd_rn(gib[j], g[0][jl][bl]));
+    const float z = sigmoid_ref(__fadd_rn(gib[H + j], g[1][jl][bl]));
+    const float n = tanhf(__fadd_rn(gib[2 * H + j], __fmul_rn(r, g[2][jl][bl])));
+    const float h = h_prev[(int64_t)b * ld_prev + j];
+    const float one_minus_z = __fadd_rn(-z, 1.0f);
+    h_out[(int64_t)b * ld_out + j] = __fadd_rn(__fmul_rn(one_minus_z, n), __fmul_rn(z, h));
 }
 
 int gate(const float* gi, const float* gh, const float* b_hh, const float* h_prev, int64_t ld_prev, float* h_out,
@@ -203,12 +224,10 @@ extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int inp
                 rc = tc_gemm_planes(w_hi, w_lo, h_hi, h_lo, (int)G, batch, hidden, 1, part, batch, G * batch, nullptr,
                                     0, device_error_word(), s, 0, nullptr, 0, 0, 0, 0, 0, S);
             if (!rc) {
-                const int64_t total = (int64_t)batch * hidden;
-                const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
                 {
                     ProfScope prof(s, KID_RNN);
-                    gru_gate_t_kernel<<<blocks, 256, 0, s>>>(git, part, S, b_hh, h_prev, ld_prev, h_out, ld_out,
-                                                             batch, hidden);
+                    gru_gate_t_kernel<<<dim3((hidden + 7) / 8, (batch + 31) / 32), 256, 0, s>>>(
+                        git, part, S, b_hh, h_prev, ld_prev, h_out, ld_out, batch, hidden);
                 }
                 if (cudaPeekAtLastError() != cudaSuccess) rc = set_status(JST_ERR_CUDA, "gru gate launch failed");
             }
