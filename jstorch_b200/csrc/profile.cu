@@ -51,6 +51,13 @@ cudaEvent_t take_event() {
 ProfScope::ProfScope(cudaStream_t s, int kernel) : s_(s), kernel_(kernel) {
     g_launches.fetch_add(1, std::memory_order_relaxed);
     if (!g_enabled.load(std::memory_order_relaxed)) return;
+    // launches being captured into a CUDA graph are not timed (their events
+    // would become graph nodes)
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+        cudaGetLastError();
+        return;
+    }
     std::lock_guard<std::mutex> lk(g_mu);
     ev0_ = take_event();
     ev1_ = take_event();
