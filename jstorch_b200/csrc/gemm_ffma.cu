@@ -290,7 +290,7 @@ int ffma_gemm_run(const GemmArgs& a, cudaStream_t s) {
     // tiles (4 x 4 per thread) otherwise.
     const long long big_tiles = (long long)((a.M + 127) / 128) * ((a.N + 127) / 128) * a.batch;
     if (big_tiles >= 148) {
-        launch_cfg<128, 128, 8, 2, 2>(p, a.batch, a.transA, a.transB, s);
+        launch_cfg<128, 128, 16, 2, 2>(p, a.batch, a.transA, a.transB, s);
         if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "ffma_gemm_kernel launch failed");
         return JST_OK;
     }
