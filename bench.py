@@ -55,6 +55,7 @@ def _tensor_peak(peaks: dict, clk: dict) -> tuple[float, str]:
     """3xTF32 roofline (bf16 dense / 2 for the TF32 rate / 3 products): the
     burst figure when the timed region ran at full clock, the sustained one
     when it ran under the power cap (clocks below max with sw_power_cap)."""
+    clk = clk or {}  # ranks other than 0 do not sample clocks
     reasons = clk.get("reasons") or []
     sm, smax = clk.get("sm_mhz"), clk.get("sm_max_mhz")
     capped = "sw_power_cap" in reasons or (sm and smax and sm < 0.95 * smax)
