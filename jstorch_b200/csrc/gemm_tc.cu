@@ -135,8 +135,9 @@ __global__ void __launch_bounds__(THREADS, C::MIN_BLOCKS)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    // grouped rasterisation: 8 tile-rows share a band so concurrently running
-    // CTAs reuse the same B panels from L2
+    // grouped rasterisation: bands of 16 tile-rows, so a wave of 148 CTAs
+    // covers about 16 x 9 tiles and the concurrently running CTAs share their
+    // A and B k-slabs in L2 (bands of 8 read 27 % more from DRAM at 8192^3)
     // CTA index = ((bidx * kslices) + slice) * tiles + tile: the CTAs of one
     // K slice run next to each other and share its operand panels in L2
     const int tiles_per_batch = p.tiles_m * p.tiles_n;
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(THREADS, C::MIN_BLOCKS)
     const int zs = blockIdx.x / tiles_per_batch;
     const int slice = zs % p.kslices;
     const int bidx = zs / p.kslices;
-    constexpr int GROUP = 8;
+    constexpr int GROUP = 16;
     const int group_span = GROUP * p.tiles_n;
     const int g = t / group_span;
     const int first_m = g * GROUP;
