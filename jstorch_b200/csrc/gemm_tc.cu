@@ -383,32 +383,49 @@ __global__ void split_rows_kernel(const float* __restrict__ src, int64_t ld, int
 }
 
 // Source MN-major: element (b, r, k) at src[b*sstride + k*ld + r]; transposed
-// through a 32 x 32 shared tile so both the read and the write are coalesced.
-__global__ void split_transpose_kernel(const float* __restrict__ src, int64_t ld, int64_t sstride, int rows,
-                                       int K, int Kp, float* __restrict__ hi, float* __restrict__ lo) {
-    __shared__ float tile[32][33];
+// through shared memory in tiles of 32 rows x 128 k.  Each thread issues its
+// 16 loads (32 consecutive rows per warp: 128-byte reads) before the one
+// barrier, then writes 4 consecutive k of a row as float4s (a warp covers 512
+// contiguous bytes of a plane row).  The tile row pitch of 129 floats keeps
+// the transposing shared-memory stores conflict-free.
+constexpr int STR = 32, STK = 128;
+__global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ src, int64_t ld,
+                                                              int64_t sstride, int rows, int K, int Kp,
+                                                              float* __restrict__ hi, float* __restrict__ lo) {
+    __shared__ float tile[STR][STK + 1];  // [row][k]
     const int b = blockIdx.z;
-    const int r0 = blockIdx.x * 32;
-    const int k0 = blockIdx.y * 32;
+    const int r0 = blockIdx.x * STR;
+    const int k0 = blockIdx.y * STK;
     const float* s = src + b * sstride;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // load phase: row fastest
+    float v[STK / 8];
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-        const int k = k0 + threadIdx.y + j;
-        const int r = r0 + threadIdx.x;
-        tile[threadIdx.y + j][threadIdx.x] = (k < K && r < rows) ? __ldg(s + (int64_t)k * ld + r) : 0.0f;
+    for (int i = 0; i < STK / 8; ++i) {
+        const int k = k0 + ty + 8 * i;
+        const int r = r0 + tx;
+        v[i] = (k < K && r < rows) ? __ldg(s + (int64_t)k * ld + r) : 0.0f;
     }
-    __syncthreads();
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-        const int r = r0 + threadIdx.y + j;
-        const int k = k0 + threadIdx.x;
-        if (r < rows && k < Kp) {
-            const float v = tile[threadIdx.x][threadIdx.y + j];
-            const float h = ptx::to_tf32(v);
-            const int64_t o = ((int64_t)b * rows + r) * Kp + k;
-            hi[o] = h;
-            lo[o] = ptx::to_tf32(v - h);
+    for (int i = 0; i < STK / 8; ++i) tile[tx][ty + 8 * i] = v[i];
+    __syncthreads();
+    // store phase: 32 float4 chunks per row, 8 rows per pass of 256 threads
+    const int c = threadIdx.x & 31, rr = threadIdx.x >> 5;
+#pragma unroll
+    for (int pass = 0; pass < STR / 8; ++pass) {
+        const int rl = rr + 8 * pass;
+        const int r = r0 + rl;
+        const int k = k0 + 4 * c;
+        if (r >= rows || k >= Kp) continue;
+        float h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float x = tile[rl][4 * c + j];
+            h[j] = ptx::to_tf32(x);
+            l[j] = ptx::to_tf32(x - h[j]);
         }
+        const int64_t o = ((int64_t)b * rows + r) * Kp + k;  // Kp % 4 == 0, k % 4 == 0: 16-byte aligned
+        *reinterpret_cast<float4*>(hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4*>(lo + o) = make_float4(l[0], l[1], l[2], l[3]);
     }
 }
 
@@ -473,9 +490,9 @@ static int launch_split(const float* src, bool kmajor, int64_t ld, int64_t sstri
         else
             split_rows_kernel<false><<<blocks, threads, 0, s>>>(src, ld, sstride, rows, K, Kp, batch, hi, lo);
     } else {
-        dim3 grid((rows + 31) / 32, (Kp + 31) / 32, batch);
+        dim3 grid((rows + STR - 1) / STR, (Kp + STK - 1) / STK, batch);
         ProfScope prof(s, KID_SPLIT_TRANSPOSE);
-        split_transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(src, ld, sstride, rows, K, Kp, hi, lo);
+        split_transpose_kernel<<<grid, 256, 0, s>>>(src, ld, sstride, rows, K, Kp, hi, lo);
     }
     return cudaPeekAtLastError() == cudaSuccess ? JST_OK : JST_ERR_CUDA;
 }
