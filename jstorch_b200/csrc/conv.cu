@@ -122,67 +122,82 @@ __global__ void permute_bcn_kernel(const float* __restrict__ src, float* __restr
 // ---- im2col fused with the 3xTF32 split (hi = rn_tf32(v), lo = rn_tf32(v - hi))
 
 // Forward operand: planes [b][n][Kp] of the column matrix of one group,
-// element (k = c*kk + tap, n) read from image channel c0 + c.  A 32 x 32 tile
-// goes through shared memory so that the image reads (along n) and the plane
-// writes (along k) are both coalesced.  A block covers 32 pixels and
-// KT_PER_BLOCK tiles of k; the (channel, tap) offsets of its k values are
-// decoded once into shared memory, so the element loop has no division.
+// element (k = c*kk + tap, n) read from image channel c0 + c.  A block covers
+// 32 pixels x 128 k values (KT_PER_BLOCK x 32): its image reads go along n
+// (one pixel per lane) into a [pixel][k] shared-memory tile with a row pitch
+// of 129 floats, and its plane writes go along k as float4 stores.  A warp's
+// store covers 4 pixels x 32 k (four 128-byte runs), which makes the tile
+// reads conflict-free: bank (n + k) mod 32 = p + 4 c8 + const over lane
+// (p, c8).  The block's k values are decoded once into a 16-byte record each
+// (image offset of the channel and tap, tap row and column offsets), so the
+// element loop has no division; a padding column k >= Kg and a pixel n >= N
+// carry a large negative row offset, so the one unsigned row check rejects
+// them.  Image offsets are 32-bit (the host routes larger images elsewhere).
 constexpr int KT_PER_BLOCK = 4;
+constexpr int IM2COL_BK = 32 * KT_PER_BLOCK;
+constexpr int OFF_ROW = -(1 << 29);  // row offset that fails every row check
+struct __align__(16) KTap {
+    int off;     // c * H * W + dh * W + dw
+    int dh, dw;  // kh * dH - pH, kw * dW - pW
+    int pad_;
+};
 __global__ void __launch_bounds__(256) im2col_split_t_kernel(const float* __restrict__ x, const Geo g, int c0, int Kg,
                                                              int Kp, float* __restrict__ hi, float* __restrict__ lo) {
-    __shared__ float tile[KT_PER_BLOCK][32][33];
-    __shared__ int64_t k_base[32 * KT_PER_BLOCK];
-    __shared__ int k_dh[32 * KT_PER_BLOCK], k_dw[32 * KT_PER_BLOCK];
+    __shared__ float tile[32][IM2COL_BK + 1];  // [pixel][k]
+    __shared__ KTap taps[IM2COL_BK];
     const int b = blockIdx.z;
-    const int n0 = blockIdx.x * 32, kb0 = blockIdx.y * 32 * KT_PER_BLOCK;
+    const int n0 = blockIdx.x * 32, kb0 = blockIdx.y * IM2COL_BK;
     const int N = g.Ho * g.Wo, kk = g.kH * g.kW, HW = g.H * g.W;
     const int tid = threadIdx.y * 32 + threadIdx.x;
-    if (tid < 32 * KT_PER_BLOCK) {
+    if (tid < IM2COL_BK) {
         const int k = kb0 + tid;
         const int c = k / kk, tap = k - c * kk;
         const int kh = tap / g.kW, kw = tap - kh * g.kW;
-        k_base[tid] = k < Kg ? (int64_t)c * HW : -1;  // -1: padding column k >= Kg
-        k_dh[tid] = kh * g.dH - g.pH;
-        k_dw[tid] = kw * g.dW - g.pW;
+        const int dh = kh * g.dH - g.pH, dw = kw * g.dW - g.pW;
+        taps[tid] = k < Kg ? KTap{(int)((unsigned)c * HW + (unsigned)(dh * g.W + dw)), dh, dw, 0}
+                           : KTap{0, OFF_ROW, 0, 0};
     }
     const float* xb = x + ((int64_t)b * g.C + c0) * HW;
     const int n = n0 + threadIdx.x;
-    const int ho = n / g.Wo, wo = n - ho * g.Wo;
-    const int hs = ho * g.sH, ws = wo * g.sW;
+    const int nc = n < N ? n : 0;
+    const int ho = nc / g.Wo, wo = nc - ho * g.Wo;
+    const int hs = n < N ? ho * g.sH : OFF_ROW, ws = wo * g.sW;
+    const unsigned p0 = (unsigned)(ho * g.sH) * g.W + ws;
     __syncthreads();
-    // every image load of the block's KT_PER_BLOCK x 32 x 32 elements is issued
-    // before the single barrier: 16 loads in flight per thread
-    float v[KT_PER_BLOCK][4];
+    // every image load of the block's 32 x 128 elements is issued before the
+    // tile barrier: 16 loads in flight per thread
+    float v[IM2COL_BK / 8];
 #pragma unroll
-    for (int kt = 0; kt < KT_PER_BLOCK; ++kt)
+    for (int i = 0; i < IM2COL_BK / 8; ++i) {
+        const KTap t = taps[threadIdx.y + 8 * i];
+        const bool ok = (unsigned)(hs + t.dh) < (unsigned)g.H && (unsigned)(ws + t.dw) < (unsigned)g.W;
+        v[i] = ok ? __ldg(xb + (p0 + (unsigned)t.off)) : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < IM2COL_BK / 8; ++i) tile[threadIdx.x][threadIdx.y + 8 * i] = v[i];
+    __syncthreads();
+    // store phase: warp w writes pixels 4w .. 4w+3, lane (p, c8) = pixel 4w + p,
+    // k = 32 q + 4 c8 .. +3 in pass q
+    const int nl = threadIdx.y * 4 + (threadIdx.x >> 3), c8 = threadIdx.x & 7;
+    const int nn = n0 + nl;
+    if (nn >= N) return;
+    float* hrow = hi + ((int64_t)b * N + nn) * Kp;
+    float* lrow = lo + ((int64_t)b * N + nn) * Kp;
+#pragma unroll
+    for (int q = 0; q < KT_PER_BLOCK; ++q) {
+        const int kl = 32 * q + 4 * c8;
+        const int k = kb0 + kl;
+        if (k >= Kp) break;
+        float h[4], l[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const int kl = kt * 32 + threadIdx.y + j * 8;
-            const int64_t base = k_base[kl];
-            const int ih = hs + k_dh[kl], iw = ws + k_dw[kl];
-            v[kt][j] = (base >= 0 && n < N && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W)
-                           ? __ldg(xb + base + ih * g.W + iw)
-                           : 0.0f;
+            const float val = tile[nl][kl + j];
+            h[j] = ptx::to_tf32(val);
+            l[j] = ptx::to_tf32(val - h[j]);
         }
-#pragma unroll
-    for (int kt = 0; kt < KT_PER_BLOCK; ++kt)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tile[kt][threadIdx.y + j * 8][threadIdx.x] = v[kt][j];
-    __syncthreads();
-#pragma unroll
-    for (int kt = 0; kt < KT_PER_BLOCK; ++kt) {
-        const int k = kb0 + kt * 32 + threadIdx.x;
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-            const int nn = n0 + threadIdx.y + j;
-            if (nn < N && k < Kp) {
-                const float val = tile[kt][threadIdx.x][threadIdx.y + j];
-                const float h = ptx::to_tf32(val);
-                const int64_t o = ((int64_t)b * N + nn) * Kp + k;
-                hi[o] = h;
-                lo[o] = ptx::to_tf32(val - h);
-            }
-        }
+        // Kp % 4 == 0, k % 4 == 0: 16-byte aligned
+        *reinterpret_cast<float4*>(hrow + k) = make_float4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<float4*>(lrow + k) = make_float4(l[0], l[1], l[2], l[3]);
     }
 }
 
@@ -356,7 +371,7 @@ int conv2d_tc(const float* input, const float* weight, const float* bias, float*
         if (rc) break;
         {
             ProfScope prof(s, KID_CONV);
-            im2col_split_t_kernel<<<dim3((N + 31) / 32, (Kp + 32 * KT_PER_BLOCK - 1) / (32 * KT_PER_BLOCK), g.B),
+            im2col_split_t_kernel<<<dim3((N + 31) / 32, (Kp + IM2COL_BK - 1) / IM2COL_BK, g.B),
                                     dim3(32, 8), 0, s>>>(input, g, grp * Ci_g, Kg, Kp, b_hi, b_lo);
         }
         if (cudaPeekAtLastError() != cudaSuccess) {
@@ -381,7 +396,9 @@ int conv2d(const float* input, const float* weight, const float* bias, float* ou
     const int64_t N = (int64_t)Ho * Wo, kk = (int64_t)kH * kW, Kg = Ci_g * kk;
     if (!fits_int(N) || !fits_int(Kg)) return set_status(JST_ERR_ARG, "conv: GEMM dimension exceeds int");
     const bool direct = kH == 1 && kW == 1 && sH == 1 && sW == 1 && pH == 0 && pW == 0 && Ho == H && Wo == W;
-    if (!direct && B > 0 && B <= 65535 && Co_g > 0 && Kg > 0 && on_tensor_cores(Co_g, (int)N, (int)Kg, B) &&
+    // the fused im2col split addresses one group's image with 32-bit offsets
+    if (!direct && B > 0 && B <= 65535 && Co_g > 0 && Kg > 0 && fits_int((int64_t)Ci_g * H * W) &&
+        on_tensor_cores(Co_g, (int)N, (int)Kg, B) &&
         tc_split_k(shape_args(Co_g, (int)N, (int)Kg, B)) == 1) {
         rc = conv2d_tc(input, weight, bias, output, Geo{B, Ci, H, W, kH, kW, sH, sW, pH, pW, dH, dW, Ho, Wo}, Co,
                        groups, s);
