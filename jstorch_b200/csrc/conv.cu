@@ -206,8 +206,9 @@ __global__ void __launch_bounds__(256) im2col_split_t_kernel(const float* __rest
 // column matrix, split as it is formed.  With a 1 x 1 geometry this is the
 // [B][C][N] -> [C][B*N] permute of the other operand.  One block row per r,
 // four consecutive k per thread (float4 stores).
-__global__ void im2col_split_rows_kernel(const float* __restrict__ x, const Geo g, int c0, int rows, int64_t BN,
-                                         int64_t Kp, float* __restrict__ hi, float* __restrict__ lo) {
+__global__ void __launch_bounds__(256) im2col_split_rows_kernel(const float* __restrict__ x, const Geo g, int c0,
+                                                                int rows, int64_t BN, int64_t Kp,
+                                                                float* __restrict__ hi, float* __restrict__ lo) {
     const int r = blockIdx.y;
     if (r >= rows) return;
     const int N = g.Ho * g.Wo, kk = g.kH * g.kW, HW = g.H * g.W;
@@ -217,26 +218,45 @@ __global__ void im2col_split_rows_kernel(const float* __restrict__ x, const Geo 
     const int64_t img = (int64_t)g.C * HW;
     float* ho_ = hi + (int64_t)r * Kp;
     float* lo_ = lo + (int64_t)r * Kp;
-    for (int64_t k4 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; k4 < Kp;
-         k4 += (int64_t)gridDim.x * blockDim.x * 4) {
-        float v[4];
-        // (b, h, w) of k4, then stepped along w without divisions
-        const int b0 = (int)(k4 / N);
-        const int n = (int)(k4 - (int64_t)b0 * N);
-        int b = b0, h = n / g.Wo, w = n - h * g.Wo;
+    int64_t k4 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (k4 >= Kp) return;
+    // (b, h, w) of the thread's first k, then advanced by the loop stride as
+    // mixed-radix digits (stride = sb images + sh rows + sw columns, with
+    // sh < Ho and sw < Wo, so each digit carries at most once)
+    const int64_t step = (int64_t)gridDim.x * blockDim.x * 4;
+    int b = (int)(k4 / N);
+    int h = (int)(k4 - (int64_t)b * N);
+    int w = h % g.Wo;
+    h /= g.Wo;
+    const int sb = (int)(step / N), srem = (int)(step - (int64_t)sb * N);
+    const int sh = srem / g.Wo, sw = srem - sh * g.Wo;
+    for (; k4 < Kp; k4 += step) {
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (w + 3 < g.Wo && k4 + 4 <= BN) {
+            // the four k lie on one output row: one row check, one base address
+            const int ih = h * g.sH + oh;
+            if ((unsigned)ih < (unsigned)g.H) {
+                const float* xr = xc + b * img + ih * g.W;
+                const int iw0 = w * g.sW + ow;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            v[j] = 0.0f;
-            if (k4 + j < BN) {
-                const int ih = h * g.sH + oh, iw = w * g.sW + ow;
-                if ((unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W)
-                    v[j] = __ldg(xc + b * img + ih * g.W + iw);
+                for (int j = 0; j < 4; ++j) {
+                    const int iw = iw0 + j * g.sW;
+                    if ((unsigned)iw < (unsigned)g.W) v[j] = __ldg(xr + iw);
+                }
             }
-            if (++w == g.Wo) {
-                w = 0;
-                if (++h == g.Ho) {
-                    h = 0;
-                    ++b;
+        } else {
+            int bb = b, hh = h, ww = w;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int ih = hh * g.sH + oh, iw = ww * g.sW + ow;
+                if (k4 + j < BN && (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W)
+                    v[j] = __ldg(xc + bb * img + ih * g.W + iw);
+                if (++ww == g.Wo) {
+                    ww = 0;
+                    if (++hh == g.Ho) {
+                        hh = 0;
+                        ++bb;
+                    }
                 }
             }
         }
@@ -248,6 +268,17 @@ __global__ void im2col_split_rows_kernel(const float* __restrict__ x, const Geo 
         }
         *reinterpret_cast<float4*>(ho_ + k4) = make_float4(hv[0], hv[1], hv[2], hv[3]);
         *reinterpret_cast<float4*>(lo_ + k4) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+        w += sw;
+        if (w >= g.Wo) {
+            w -= g.Wo;
+            ++h;
+        }
+        h += sh;
+        if (h >= g.Ho) {
+            h -= g.Ho;
+            ++b;
+        }
+        b += sb;
     }
 }
 
