@@ -284,8 +284,15 @@ __global__ void __launch_bounds__(THREADS, C::MIN_BLOCKS)
                 ptx::tmem_ld_32x32b_x32(taddr + D_HI_COL, r);
                 ptx::tmem_ld_32x32b_x32(taddr + D_LO_COL, rl);
                 ptx::tmem_ld_wait();
+                // A non-finite D_hi (an Inf or NaN operand, or overflow) is the
+                // result: D_lo then holds Inf * 0 = NaN from the cross terms of
+                // an infinite operand (its lo part is Inf - Inf), which would
+                // turn an Inf result into NaN.
 #pragma unroll
-                for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(rl[j]));
+                for (int j = 0; j < 32; ++j) {
+                    const uint32_t h = r[j];
+                    if ((h & 0x7f800000u) != 0x7f800000u) r[j] = __float_as_uint(__uint_as_float(h) + __uint_as_float(rl[j]));
+                }
                 if (row_bias) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + rbias);

@@ -370,3 +370,56 @@ def test_in_kernel_a_split_matches_plane_path(jst, M, N, K, batch, bcast):
     np.testing.assert_array_equal(C, c_ref.cpu().numpy())
     for i in range(batch):
         _check(A[0 if bcast else i], B[i], C[i], rows=np.arange(0, M, 5))
+
+
+def _non_finite_operands(rng, M, N, K):
+    A = _rand(rng, M, K)
+    B = _rand(rng, K, N)
+    A[3, 5], A[7, 11], A[9, 2] = np.inf, -np.inf, np.nan
+    B[4, 13], B[6, N - 1] = np.inf, np.nan
+    return A, B
+
+
+def _check_non_finite(A, B, C):
+    """Every element has the IEEE class of the exact product (the oracle's
+    sequential fp64 sum over the same fp32 inputs): +Inf, -Inf and NaN where
+    it has them; the elements whose row of A and column of B are all finite
+    keep the path's bound."""
+    ref = oracle.gemm_f64(A, B)
+    for cls in (np.isnan, np.isposinf, np.isneginf):
+        np.testing.assert_array_equal(cls(C), cls(ref))
+    r = np.flatnonzero(np.isfinite(A).all(axis=1))
+    c = np.flatnonzero(np.isfinite(B).all(axis=0))
+    _check(A[r], B[:, c], C[np.ix_(r, c)], rows=np.arange(0, r.size, 3))
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("M,N,K", [
+    (512, 1024, 512),   # 128 x 256 tile, operands split by the split passes
+    (256, 64, 512),     # narrow tile, A split inside the kernel
+    (128, 300, 20000),  # split-K slices and the reduce
+])
+def test_non_finite_operands(jst, kernel, M, N, K):
+    """Inf and NaN operands (matmul.cu:11-37: cuBLAS fp32 GEMM, whose
+    products and sums follow IEEE): a row of A holding +-Inf gives +-Inf by
+    the signs of the matching row of B, NaN gives NaN, and an infinite row
+    meeting an infinite column of the opposite sign gives NaN.  The 3xTF32
+    cross terms of an infinite operand are Inf * 0 = NaN; the kernel returns
+    the hi * hi accumulator wherever that is non-finite."""
+    import torch
+    rng = np.random.default_rng(M + N + K)
+    A, B = _non_finite_operands(rng, M, N, K)
+    c = jst.gemm(_dev(A), _dev(B), kernel=kernel)
+    torch.cuda.synchronize()
+    _check_non_finite(A, B, c.cpu().numpy())
+
+
+def test_non_finite_operands_host_pipeline(jst):
+    """The same through torch.matmul on host arrays (the blocked, pipelined
+    tensor-core path)."""
+    rng = np.random.default_rng(5)
+    M, K, N = 2500, 300, 2300
+    assert jst.select_kernel(M, N, K) == "tc3xtf32"
+    A, B = _non_finite_operands(rng, M, N, K)
+    A[2400, 7] = np.inf  # in the ragged last row block
+    _check_non_finite(A, B, jst.torch.matmul(A, B, M, K, N).reshape(M, N))
