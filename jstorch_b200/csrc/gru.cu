@@ -15,10 +15,11 @@
 //   * at the first step with no initial state, gh = b_hh and the GEMM is
 //     skipped;
 //   * for realistic sizes the recurrent product runs on the tensor cores as
-//     ghT = W_hh . h^T: W_hh is split into tf32 planes once per call, each
-//     step splits only h, the GEMM is cut into K-slices so its few output
-//     tiles fill the SMs, and one kernel sums the slices in order, adds b_hh
-//     and applies the gates.
+//     ghT = W_hh . h^T: W_hh is split into tf32 planes once per call, the
+//     GEMM is cut into K-slices so its few output tiles fill the SMs, and one
+//     kernel sums the slices in order, adds b_hh, applies the gates and
+//     writes h' both into the output sequence and as the tf32 hi / lo planes
+//     the next step's GEMM reads (two launches per step).
 // The gate arithmetic follows the reference op by op in fp32: sigmoid as
 // 1 / (1 + __expf(-x)) and tanhf (native/ops/kernels.cuh:48-49), (1 - z) as
 // (-z) + 1, and h' = ((1 - z) * n) + (z * h) with each product rounded.
@@ -29,6 +30,7 @@
 
 #include "../../include/jstorch_rnn.h"
 #include "gemm_internal.h"
+#include "ptx.cuh"
 
 namespace jst {
 namespace {
@@ -72,11 +74,14 @@ __global__ void gru_gate_kernel(const float* __restrict__ gi, const float* __res
 // unit (128-byte reads of the [row][batch] partials), transposes through
 // shared memory, then applies the gates with 8 threads along the hidden units
 // per batch row (whole 32-byte sectors of gi, h and h').  Same arithmetic as
-// gru_gate_kernel.
+// gru_gate_kernel.  With nh_hi set it also writes the 3xTF32 split of h'
+// into the [batch][Kp] planes of the next step's GEMM (the values the split
+// pass would write; this step's GEMM has finished reading them).
 __global__ void __launch_bounds__(256) gru_gate_t_kernel(const float* __restrict__ gi, const float* __restrict__ part,
                                                          int slices, const float* __restrict__ b_hh,
                                                          const float* __restrict__ h_prev, int64_t ld_prev,
-                                                         float* __restrict__ h_out, int64_t ld_out, int batch, int H) {
+                                                         float* __restrict__ h_out, int64_t ld_out, int batch, int H,
+                                                         float* __restrict__ nh_hi, float* __restrict__ nh_lo, int Kp) {
     __shared__ float g[3][8][33];  // [gate][hidden unit][batch row]
     const int j0 = blockIdx.x * 8, b0 = blockIdx.y * 32;
     const int64_t plane = 3LL * H * batch;
@@ -115,7 +120,13 @@ __global__ void __launch_bounds__(256) gru_gate_t_kernel(const float* __restrict
     const float n = tanhf(__fadd_rn(gib[2 * H + j], __fmul_rn(r, g[2][jl][bl])));
     const float h = h_prev[(int64_t)b * ld_prev + j];
     const float one_minus_z = __fadd_rn(-z, 1.0f);
-    h_out[(int64_t)b * ld_out + j] = __fadd_rn(__fmul_rn(one_minus_z, n), __fmul_rn(z, h));
+    const float hv = __fadd_rn(__fmul_rn(one_minus_z, n), __fmul_rn(z, h));
+    h_out[(int64_t)b * ld_out + j] = hv;
+    if (nh_hi) {
+        const float hi = ptx::to_tf32(hv);
+        nh_hi[(int64_t)b * Kp + j] = hi;
+        nh_lo[(int64_t)b * Kp + j] = ptx::to_tf32(hv - hi);
+    }
 }
 
 int gate(const float* gi, const float* gh, const float* b_hh, const float* h_prev, int64_t ld_prev, float* h_out,
@@ -212,6 +223,7 @@ extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int inp
     if (!rc && tc) rc = tc_split(w_hh, 1, hidden, 0, (int)G, hidden, 1, w_hi, w_lo, s);
     const float* h_prev = h0;  // row stride `hidden` for h0, ld_out for rows of `out`
     int64_t ld_prev = hidden;
+    bool h_split = false;  // h_hi / h_lo hold the split of h_prev
     for (int step = 0; step < seq && !rc; ++step) {
         const int t = reverse ? seq - 1 - step : step;
         float* h_out = out + (int64_t)t * batch * ld_out;
@@ -219,19 +231,23 @@ extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int inp
         if (h_prev && tc) {
             // nn.js:481 as ghT[3H][batch] = W_hh . h^T on the tensor cores, split over K,
             // the slices summed with b_hh and the gates in one kernel
-            rc = tc_split(h_prev, 1, ld_prev, 0, batch, hidden, 1, h_hi, h_lo, s);
+            if (!h_split) rc = tc_split(h_prev, 1, ld_prev, 0, batch, hidden, 1, h_hi, h_lo, s);
             if (!rc)
                 rc = tc_gemm_planes(w_hi, w_lo, h_hi, h_lo, (int)G, batch, hidden, 1, part, batch, G * batch, nullptr,
                                     0, device_error_word(), s, 0, nullptr, 0, 0, 0, 0, 0, S);
             if (!rc) {
                 {
                     ProfScope prof(s, KID_RNN);
+                    const bool more = step + 1 < seq;
                     gru_gate_t_kernel<<<dim3((hidden + 7) / 8, (batch + 31) / 32), 256, 0, s>>>(
-                        git, part, S, b_hh, h_prev, ld_prev, h_out, ld_out, batch, hidden);
+                        git, part, S, b_hh, h_prev, ld_prev, h_out, ld_out, batch, hidden, more ? h_hi : nullptr,
+                        more ? h_lo : nullptr, Kp);
+                    h_split = more;
                 }
                 if (cudaPeekAtLastError() != cudaSuccess) rc = set_status(JST_ERR_CUDA, "gru gate launch failed");
             }
         } else {
+            h_split = false;
             const float* ghp = nullptr;
             if (h_prev) {  // nn.js:481
                 rc = nt_gemm(h_prev, ld_prev, w_hh, b_hh, gh, batch, (int)G, hidden, s);

@@ -42,6 +42,7 @@ def _run(seq, batch, inp, H, layers, bidir, with_h0, batch_first=False, seed=0):
     (12, 16, 64, 128, 2, True, True),    # stacked, bidirectional, given h0
     (40, 64, 256, 512, 1, False, True),  # recurrent GEMMs of a realistic size (tensor-core step)
     (10, 24, 96, 512, 2, True, True),    # tensor-core step, bidirectional, batch not a multiple of 4
+    (7, 24, 40, 510, 1, False, True),    # tensor-core step, H not a multiple of 4 (zero plane padding)
     (3, 1, 1, 1, 1, True, False),        # the degenerate one-unit case
 ])
 def test_gru_against_oracle(seq, batch, inp, H, layers, bidir, with_h0):
