@@ -53,11 +53,14 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
 // kslices > 1: split K into that many slices; C then receives the raw partial
 // products part[slice][batch][M][N] (ldc = N, strideC = M * N, no epilogue) for
 // splitk_reduce_run to combine.
+// pdl: launch as a programmatic dependent of the previous kernel on `s` (the
+// kernel's set-up overlaps that kernel's tail; it waits for its completion
+// before touching global memory).
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
                    cudaStream_t s, int mc_store = 0, const float* aux = nullptr, int64_t ld_aux = 0,
                    int64_t stride_aux = 0, int bias_row = 0, int a_bcast = 0, int b_bcast = 0, int kslices = 1,
-                   int split_a = 0, int64_t lda_raw = 0, int64_t strideA_raw = 0);
+                   int split_a = 0, int64_t lda_raw = 0, int64_t strideA_raw = 0, int pdl = 0);
 // Tile width (64, 128 or 256 columns of C per CTA) the tensor-core kernel uses for a shape.
 int tc_pick_bn(int M, int N, int K);
 // split-K slices the tensor-core path uses for `a` (1: none)

@@ -177,6 +177,10 @@ __global__ void __launch_bounds__(THREADS, C::MIN_BLOCKS)
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Launched as a programmatic dependent (pdl), the set-up above overlapped
+    // the previous kernel; no global memory is touched before this wait.
+    ptx::griddep_wait();
+    ptx::griddep_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -567,7 +571,7 @@ int tc_split(const float* src, int kmajor, int64_t ld, int64_t sstride, int rows
 // Launch one configuration; its shared-memory opt-in is set once per device.
 template <class Cf>
 static int launch_cfg(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
-                      const CUtensorMap& b_lo, const tc::Params& p, unsigned grid, cudaStream_t s) {
+                      const CUtensorMap& b_lo, const tc::Params& p, unsigned grid, cudaStream_t s, bool pdl) {
     static bool attr_set[64] = {};
     static std::mutex mu;
     int dev = 0;
@@ -583,7 +587,22 @@ static int launch_cfg(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CU
     }
     {
         ProfScope prof(s, KID_TC_GEMM);
-        tc::tc_gemm_kernel<Cf><<<grid, tc::THREADS, Cf::SMEM_BYTES, s>>>(a_hi, a_lo, b_hi, b_lo, p);
+        if (pdl) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(grid);
+            cfg.blockDim = dim3(tc::THREADS);
+            cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
+            cfg.stream = s;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[0].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<Cf>, a_hi, a_lo, b_hi, b_lo, p) != cudaSuccess)
+                return set_status(JST_ERR_CUDA, "tc_gemm_kernel launch failed");
+        } else {
+            tc::tc_gemm_kernel<Cf><<<grid, tc::THREADS, Cf::SMEM_BYTES, s>>>(a_hi, a_lo, b_hi, b_lo, p);
+        }
     }
     if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "tc_gemm_kernel launch failed");
     return JST_OK;
@@ -592,7 +611,8 @@ static int launch_cfg(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CU
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
                    cudaStream_t s, int mc_store, const float* aux, int64_t ld_aux, int64_t stride_aux, int bias_row,
-                   int a_bcast, int b_bcast, int kslices, int split_a, int64_t lda_raw, int64_t strideA_raw) {
+                   int a_bcast, int b_bcast, int kslices, int split_a, int64_t lda_raw, int64_t strideA_raw,
+                   int pdl) {
     using namespace tc;
     const int Kp = (K + 3) & ~3;
     const int num_kb = (K + BK - 1) / BK;
@@ -629,9 +649,9 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * batch * kslices;
     if (grid > 0x7fffffff) return set_status(JST_ERR_ARG, "tc: too many tiles");
     int rc;
-    if (bn == 256) rc = launch_cfg<CfgWide>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s);
-    else if (bn == 128) rc = launch_cfg<CfgMid>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s);
-    else rc = launch_cfg<CfgNarrow>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s);
+    if (bn == 256) rc = launch_cfg<CfgWide>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s, pdl != 0);
+    else if (bn == 128) rc = launch_cfg<CfgMid>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s, pdl != 0);
+    else rc = launch_cfg<CfgNarrow>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s, pdl != 0);
     return rc;
 }
 

@@ -83,6 +83,7 @@ __global__ void __launch_bounds__(256) gru_gate_t_kernel(const float* __restrict
                                                          float* __restrict__ h_out, int64_t ld_out, int batch, int H,
                                                          float* __restrict__ nh_hi, float* __restrict__ nh_lo, int Kp) {
     __shared__ float g[3][8][33];  // [gate][hidden unit][batch row]
+    ptx::griddep_wait();  // launched as a programmatic dependent of the step's GEMM
     const int j0 = blockIdx.x * 8, b0 = blockIdx.y * 32;
     const int64_t plane = 3LL * H * batch;
     const int t = threadIdx.x;
@@ -234,17 +235,29 @@ extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int inp
             if (!h_split) rc = tc_split(h_prev, 1, ld_prev, 0, batch, hidden, 1, h_hi, h_lo, s);
             if (!rc)
                 rc = tc_gemm_planes(w_hi, w_lo, h_hi, h_lo, (int)G, batch, hidden, 1, part, batch, G * batch, nullptr,
-                                    0, device_error_word(), s, 0, nullptr, 0, 0, 0, 0, 0, S);
+                                    0, device_error_word(), s, 0, nullptr, 0, 0, 0, 0, 0, S, 0, 0, 0, /*pdl=*/1);
             if (!rc) {
                 {
                     ProfScope prof(s, KID_RNN);
                     const bool more = step + 1 < seq;
-                    gru_gate_t_kernel<<<dim3((hidden + 7) / 8, (batch + 31) / 32), 256, 0, s>>>(
-                        git, part, S, b_hh, h_prev, ld_prev, h_out, ld_out, batch, hidden, more ? h_hi : nullptr,
-                        more ? h_lo : nullptr, Kp);
+                    // a programmatic dependent of the GEMM: its blocks are
+                    // scheduled while the GEMM drains and wait for it in-kernel
+                    cudaLaunchConfig_t cfg = {};
+                    cfg.gridDim = dim3((hidden + 7) / 8, (batch + 31) / 32);
+                    cfg.blockDim = dim3(256);
+                    cfg.stream = s;
+                    cudaLaunchAttribute attr[1];
+                    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+                    attr[0].val.programmaticStreamSerializationAllowed = 1;
+                    cfg.attrs = attr;
+                    cfg.numAttrs = 1;
+                    if (cudaLaunchKernelEx(&cfg, gru_gate_t_kernel, git, (const float*)part, S, b_hh, h_prev, ld_prev,
+                                           h_out, ld_out, batch, hidden, more ? h_hi : nullptr,
+                                           more ? h_lo : nullptr, Kp) != cudaSuccess)
+                        rc = set_status(JST_ERR_CUDA, "gru gate launch failed");
                     h_split = more;
                 }
-                if (cudaPeekAtLastError() != cudaSuccess) rc = set_status(JST_ERR_CUDA, "gru gate launch failed");
+                if (!rc && cudaPeekAtLastError() != cudaSuccess) rc = set_status(JST_ERR_CUDA, "gru gate launch failed");
             }
         } else {
             h_split = false;

@@ -101,6 +101,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
         : "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch
+// Wait until the grids this one depends on (launched before it with the
+// programmatic-serialization attribute) have completed and their writes are
+// visible; returns at once for a grid launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next grid on the stream, if it was launched with the attribute, be
+// scheduled now (it still waits for this grid's completion in griddep_wait).
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 template <uint32_t NCOLS>
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem) {  // whole warp
