@@ -676,12 +676,15 @@ static int tc_gemm_launch(const GemmArgs& a, void* workspace, uint32_t* err, cud
     // op(B)^T rows are N: K-major when B is stored [N, K] (transB).
     rc = tc_split(a.B, a.transB, a.ldb, a.strideB, a.N, a.K, bb, b_hi, b_lo, s);
     if (rc) return rc;
+    // the GEMM follows the B split on `s`: launched as its programmatic
+    // dependent, its set-up overlaps the split's tail
     const int S = tc_split_k(a);
     if (S <= 1)
         return tc_gemm_planes(ah, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, a.C, a.ldc, a.strideC, a.bias, a.relu, err,
-                              s, 0, a.aux, a.ld_aux, a.stride_aux, a.bias_row, abc, bbc, 1, sa, a.lda, a.strideA);
+                              s, 0, a.aux, a.ld_aux, a.stride_aux, a.bias_row, abc, bbc, 1, sa, a.lda, a.strideA,
+                              /*pdl=*/1);
     rc = tc_gemm_planes(ah, a_lo, b_hi, b_lo, a.M, a.N, a.K, a.batch, part, a.N, (int64_t)a.M * a.N, nullptr, 0, err,
-                        s, 0, nullptr, 0, 0, 0, abc, bbc, S, sa, a.lda, a.strideA);
+                        s, 0, nullptr, 0, 0, 0, abc, bbc, S, sa, a.lda, a.strideA, /*pdl=*/1);
     if (rc) return rc;
     return splitk_reduce_run(splitk_reduce_args(a, part, S), s);
 }
