@@ -88,7 +88,6 @@ def gpu_sharded(rank: int, world: int, port: int, out_q) -> None:
         torch.cuda.set_device(rank)
         d = _init_pg(rank, world, port)
         comm = jdist.Comm.from_process_group(timeout_s=30.0)
-        # n = 1024: the multicast path sends B in 4 column panels of 256
         m_local, k, n, chunk = 768, 320, 1024, 256
         plan = jdist.row_plan(world, rank, m_local, chunk)
         a_local = np.concatenate([synth.matrix(4, synth.A, blk.rows, k, "uniform", row0=blk.global_row0)
@@ -138,9 +137,28 @@ def gpu_sharded(rank: int, world: int, port: int, out_q) -> None:
             comm.sync(st)
             err3, _ = oracle.max_rel_err(a_full, b_host, cs.cpu().numpy(), ref)
             msgs.append(f"fused multicast err {err3:.2e}")
-            ok = ok and err3 <= 2e-6
+            ok = ok and err3 <= 2e-6 and np.array_equal(b.cpu().numpy(), b_host)  # B arrived in place too
         finally:
             buf.free()
+        # fused path, ragged: K not a multiple of 4, last panel of B 232 columns wide
+        k2, n2 = 317, 1000
+        a2_local = np.concatenate([synth.matrix(6, synth.A, blk.rows, k2, "normal", row0=blk.global_row0)
+                                   for blk in plan])
+        b2_host = synth.matrix(6, synth.B, k2, n2, "normal")
+        b2 = torch.from_numpy(b2_host if rank == 0 else np.zeros_like(b2_host)).cuda()
+        buf2 = comm.symm_alloc(m_local * world * n2 * 4)
+        try:
+            cs2 = buf2.tensor((m_local * world, n2))
+            cs2.fill_(float("nan"))
+            a2 = torch.from_numpy(a2_local).cuda()  # alive until the sync: read on the library's own streams too
+            comm.gemm_rowsharded(a2, b2, cs2, chunk, root=0, stream=st)
+            comm.sync(st)
+            a2_full = synth.matrix(6, synth.A, m_local * world, k2, "normal")
+            err5, _ = oracle.max_rel_err(a2_full, b2_host, cs2.cpu().numpy(), oracle.gemm_f64(a2_full, b2_host))
+            msgs.append(f"fused multicast ragged err {err5:.2e}")
+            ok = ok and err5 <= 2e-6 and np.array_equal(b2.cpu().numpy(), b2_host)
+        finally:
+            buf2.free()
         comm.destroy()
         d.destroy_process_group()
         out_q.put((rank, ("ok " if ok else "FAIL ") + "; ".join(msgs)))
