@@ -45,6 +45,9 @@ int nccl_error(jst_comm* c, ncclResult_t r, const char* what) {
 }
 
 // Wait (on the host) until the communicator has no operation in progress.
+// Polls with a yield for the first 2 ms (an enqueue usually settles within
+// tens of microseconds, and the caller's next launches wait for it), then
+// every 200 us up to the communicator's deadline.
 int nccl_settle(jst_comm* c, ncclResult_t r, const char* what) {
     if (r == ncclSuccess) return JST_OK;
     if (r != ncclInProgress) return nccl_error(c, r, what);
@@ -54,6 +57,10 @@ int nccl_settle(jst_comm* c, ncclResult_t r, const char* what) {
         if (ncclCommGetAsyncError(c->nccl, &st) != ncclSuccess) return nccl_error(c, st, what);
         if (st != ncclInProgress) break;
         const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (el < 2e-3) {
+            std::this_thread::yield();
+            continue;
+        }
         if (el > c->timeout_s) {
             ncclCommAbort(c->nccl);
             c->nccl = nullptr;
