@@ -25,6 +25,7 @@
 #include <cstdint>
 
 #include "gemm_internal.h"
+#include "ptx.cuh"
 
 namespace jst {
 namespace ffma {
@@ -60,6 +61,11 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
 
     __shared__ __align__(16) float As[2][BK][BM + PAD];
     __shared__ __align__(16) float Bs[2][BK][BN + PAD];
+
+    // launched as a programmatic dependent: wait for the previous kernel's
+    // writes, then let the next kernel (the split-K reduce) be scheduled
+    ptx::griddep_wait();
+    ptx::griddep_launch_dependents();
 
     const int tid = threadIdx.x;
     const int tx = tid % TX;
@@ -260,10 +266,12 @@ static void launch_cfg(const Params& p, int batch, bool TA, bool TB, cudaStream_
     constexpr int threads = (BM / (4 * RM)) * (BN / (4 * RN));
     dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM, batch * p.kslices);
     ProfScope prof(s, KID_FFMA_GEMM);
-    if (!TA && !TB) ffma_gemm_kernel<BM, BN, BK, RM, RN, false, false><<<grid, threads, 0, s>>>(p);
-    else if (!TA && TB) ffma_gemm_kernel<BM, BN, BK, RM, RN, false, true><<<grid, threads, 0, s>>>(p);
-    else if (TA && !TB) ffma_gemm_kernel<BM, BN, BK, RM, RN, true, false><<<grid, threads, 0, s>>>(p);
-    else ffma_gemm_kernel<BM, BN, BK, RM, RN, true, true><<<grid, threads, 0, s>>>(p);
+    // a programmatic dependent of whatever precedes it on the stream (the
+    // kernel waits for it before its first load)
+    if (!TA && !TB) launch_dependent(ffma_gemm_kernel<BM, BN, BK, RM, RN, false, false>, grid, dim3(threads), 0, s, p);
+    else if (!TA && TB) launch_dependent(ffma_gemm_kernel<BM, BN, BK, RM, RN, false, true>, grid, dim3(threads), 0, s, p);
+    else if (TA && !TB) launch_dependent(ffma_gemm_kernel<BM, BN, BK, RM, RN, true, false>, grid, dim3(threads), 0, s, p);
+    else launch_dependent(ffma_gemm_kernel<BM, BN, BK, RM, RN, true, true>, grid, dim3(threads), 0, s, p);
 }
 
 static bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }

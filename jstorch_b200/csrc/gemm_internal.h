@@ -26,6 +26,34 @@ struct GemmArgs {
 // Check a public descriptor and normalise it into `a` (no device work).
 int validate_gemm_desc(const jst_gemm_desc* d, GemmArgs* a);
 
+// Whether launches on `s` may be programmatic dependents: not while `s` is
+// being captured into a CUDA graph (a captured MLP step measured no faster
+// with programmatic edges than with plain ones).
+inline bool dependent_launch_ok(cudaStream_t s) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    return cudaStreamIsCapturing(s, &st) == cudaSuccess && st == cudaStreamCaptureStatusNone;
+}
+
+// Launch `kernel` as a programmatic dependent of the previous kernel on `s`:
+// its blocks may be scheduled while that kernel drains, and the kernel must
+// execute griddepcontrol.wait before touching global memory.  A plain launch
+// under stream capture.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                    Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent_launch_ok(s) ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Stream-ordered scratch from the library's per-device pool (checks the device first).
 int workspace_alloc(size_t bytes, cudaStream_t s, void** out);
 int workspace_free(void* p, cudaStream_t s);

@@ -588,17 +588,8 @@ static int launch_cfg(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CU
     {
         ProfScope prof(s, KID_TC_GEMM);
         if (pdl) {
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(grid);
-            cfg.blockDim = dim3(tc::THREADS);
-            cfg.dynamicSmemBytes = Cf::SMEM_BYTES;
-            cfg.stream = s;
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-            attr[0].val.programmaticStreamSerializationAllowed = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            if (cudaLaunchKernelEx(&cfg, tc::tc_gemm_kernel<Cf>, a_hi, a_lo, b_hi, b_lo, p) != cudaSuccess)
+            if (launch_dependent(tc::tc_gemm_kernel<Cf>, dim3(grid), dim3(tc::THREADS), Cf::SMEM_BYTES, s, a_hi, a_lo,
+                                 b_hi, b_lo, p) != cudaSuccess)
                 return set_status(JST_ERR_CUDA, "tc_gemm_kernel launch failed");
         } else {
             tc::tc_gemm_kernel<Cf><<<grid, tc::THREADS, Cf::SMEM_BYTES, s>>>(a_hi, a_lo, b_hi, b_lo, p);

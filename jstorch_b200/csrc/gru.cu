@@ -242,18 +242,9 @@ extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int inp
                     const bool more = step + 1 < seq;
                     // a programmatic dependent of the GEMM: its blocks are
                     // scheduled while the GEMM drains and wait for it in-kernel
-                    cudaLaunchConfig_t cfg = {};
-                    cfg.gridDim = dim3((hidden + 7) / 8, (batch + 31) / 32);
-                    cfg.blockDim = dim3(256);
-                    cfg.stream = s;
-                    cudaLaunchAttribute attr[1];
-                    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-                    attr[0].val.programmaticStreamSerializationAllowed = 1;
-                    cfg.attrs = attr;
-                    cfg.numAttrs = 1;
-                    if (cudaLaunchKernelEx(&cfg, gru_gate_t_kernel, git, (const float*)part, S, b_hh, h_prev, ld_prev,
-                                           h_out, ld_out, batch, hidden, more ? h_hi : nullptr,
-                                           more ? h_lo : nullptr, Kp) != cudaSuccess)
+                    if (launch_dependent(gru_gate_t_kernel, dim3((hidden + 7) / 8, (batch + 31) / 32), dim3(256), 0, s,
+                                         git, (const float*)part, S, b_hh, h_prev, ld_prev, h_out, ld_out, batch,
+                                         hidden, more ? h_hi : nullptr, more ? h_lo : nullptr, Kp) != cudaSuccess)
                         rc = set_status(JST_ERR_CUDA, "gru gate launch failed");
                     h_split = more;
                 }

@@ -9,6 +9,7 @@
 #include <algorithm>
 
 #include "gemm_internal.h"
+#include "ptx.cuh"
 
 namespace jst {
 namespace {
@@ -16,6 +17,7 @@ namespace {
 // One thread per W consecutive columns of a row: W = 4 (float4) when N % 4 == 0.
 template <int W>
 __global__ void splitk_reduce_kernel(const SplitKReduce r) {
+    ptx::griddep_wait();  // launched as a programmatic dependent of the GEMM that wrote the partials
     const int nw = r.N / W;
     const int64_t total = (int64_t)r.batch * r.M * nw;
     const int64_t plane = (int64_t)r.batch * r.M * r.N;
@@ -69,8 +71,8 @@ int splitk_reduce_run(const SplitKReduce& r, cudaStream_t s) {
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
     {
         ProfScope prof(s, KID_SPLITK_REDUCE);
-        if (w4) splitk_reduce_kernel<4><<<blocks, 256, 0, s>>>(r);
-        else splitk_reduce_kernel<1><<<blocks, 256, 0, s>>>(r);
+        if (w4) launch_dependent(splitk_reduce_kernel<4>, dim3(blocks), dim3(256), 0, s, r);
+        else launch_dependent(splitk_reduce_kernel<1>, dim3(blocks), dim3(256), 0, s, r);
     }
     return cudaPeekAtLastError() == cudaSuccess ? JST_OK : set_status(JST_ERR_CUDA, "split-K reduce launch failed");
 }
