@@ -34,6 +34,31 @@ def test_gemm_matches_numpy_f64(ta, tb, M, N, K):
     np.testing.assert_allclose(got, ref, rtol=1e-12, atol=1e-12)
 
 
+def test_gemm_non_finite_operands_follow_ieee():
+    """The oracle's sequential fp64 sum gives the IEEE class of every element
+    for Inf / NaN operands (the reference the non-finite GPU tests compare
+    with), checked against an element-by-element fp64 sum in Python."""
+    A = _rand(9, 12)
+    B = _rand(12, 7)
+    A[2, 3], A[4, 5], A[6, 1] = np.inf, -np.inf, np.nan
+    B[3, 2], B[8, 6] = -np.inf, np.nan
+    B[5, 4] = 0.0  # -Inf * 0 = NaN in row 4
+    got = oracle.gemm_f64(A, B)
+    exp = np.empty((9, 7))
+    with np.errstate(invalid="ignore", over="ignore"):
+        for i in range(9):
+            for j in range(7):
+                acc = 0.0
+                for k in range(12):
+                    acc += float(A[i, k]) * float(B[k, j])
+                exp[i, j] = acc
+    for cls in (np.isnan, np.isposinf, np.isneginf):
+        np.testing.assert_array_equal(cls(got), cls(exp))
+    fin = np.isfinite(exp)
+    np.testing.assert_allclose(got[fin], exp[fin], rtol=1e-12, atol=1e-12)
+    assert np.isnan(got[4, 4]) and np.isnan(got[6]).all() and np.isinf(got[2, 0])
+
+
 def test_gemm_batch_bias_relu_rows():
     A = _rand(3, 20, 7)
     B = _rand(3, 7, 9)
