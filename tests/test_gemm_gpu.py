@@ -423,3 +423,26 @@ def test_non_finite_operands_host_pipeline(jst):
     A, B = _non_finite_operands(rng, M, N, K)
     A[2400, 7] = np.inf  # in the ragged last row block
     _check_non_finite(A, B, jst.torch.matmul(A, B, M, K, N).reshape(M, N))
+
+
+@pytest.mark.parametrize("kernel,M,N,K", [
+    ("ffma", 256, 1024, 1024),     # FFMA with split-K and the reduce
+    ("tc3xtf32", 1024, 1024, 1024),  # operand splits, then the tensor-core kernel
+    ("tc3xtf32", 256, 512, 4096),  # tensor cores with split-K and the reduce
+])
+def test_operands_written_by_the_previous_kernel(jst, kernel, M, N, K):
+    """A GEMM queued right behind kernels that write its operands, and
+    followed at once by a kernel that reads C, with no synchronisation in
+    between: every launch of the path that is a programmatic dependent waits
+    for the previous grid, so each product sees the values just written."""
+    import torch
+    a = torch.empty((M, K), device="cuda")
+    b = torch.empty((K, N), device="cuda")
+    c = torch.empty((M, N), device="cuda")
+    checks = []
+    for v in (1.0, 2.0, 3.0, 4.0):
+        a.fill_(v)
+        b.fill_(0.5)
+        jst.gemm(a, b, out=c, kernel=kernel)
+        checks.append((c == v * 0.5 * K).all())  # exact: every product and sum is representable
+    assert all(bool(x) for x in checks)
