@@ -105,9 +105,10 @@ int jst_gemm_select_kernel(const jst_gemm_desc* d);
  * jst_gemm_tc_noalloc -- the tensor-core (3 x TF32) GEMM of jst_gemm_ex
  * without any device allocation.  No counterpart in the reference.
  *
- * For callers that must not allocate device memory: code running while a
- * CUDA graph is being captured, hosts whose device memory belongs to another
- * allocator, and embedders that budget all device memory up front.
+ * For callers that cannot call cudaMalloc: hosts whose device memory belongs
+ * to another allocator that forbids side allocations, embedders that budget
+ * all device memory up front, and latency-critical code that cannot afford
+ * cudaMalloc / cudaFree (they may synchronise the whole device).
  * jst_gemm_ex takes its scratch (the hi/lo split planes) from a pool it
  * allocates; this entry point uses a fixed 64 MiB file-scope device array
  * instead, and calls no cudaMalloc, cudaFree or other allocating routine.
@@ -115,15 +116,20 @@ int jst_gemm_select_kernel(const jst_gemm_desc* d);
  *     (`kernel` must be AUTO or TC3XTF32).  The caller passes A, B, C, bias.
  *   - Limit: the tensor-core path's scratch must fit 64 MiB: hi/lo planes of
  *     2 * Kp * (M * Ba + N * Bb) * 4 bytes (Kp = K rounded up to a multiple
- *     of 4; Ba, Bb = batch, or 1 for an operand with batch stride 0), plus
- *     S * batch * M * N * 4 bytes of split-K partials when the output tiles
- *     fill less than half the SMs (e.g. 2048^3 fits); larger requests return
- *     JST_ERR_ARG without launching.
+ *     of 4; Ba, Bb = batch, or 1 for an operand with batch stride 0; Ba = 0
+ *     when the kernel splits a K-major A itself, as it does for outputs at
+ *     most 128 columns wide or K <= 256), plus S * batch * M * N * 4 bytes of
+ *     split-K partials when the output tiles fill less than half the SMs
+ *     (e.g. 2048^3 fits exactly); larger requests return JST_ERR_ARG without
+ *     launching.
  *   - The array exists once per device, for the life of the process, and is
  *     shared by all calls: calls whose work overlaps on the GPU (different
  *     streams or threads) race and must be serialised by the caller.
  *   - The first call on a device looks up the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *     cudaDeviceReset() is not supported after that (the address is cached).
+ *   - A pipeline wait that timed out is reported by jst_device_error(), as on
+ *     the allocating path.
  */
 int jst_gemm_tc_noalloc(const jst_gemm_desc* d);
 
@@ -182,8 +188,19 @@ int jst_copy_d2h(void* dst_host, const void* src_device, size_t bytes, jst_strea
  * Kernels never trap: a pipeline wait that exceeds its bound sets a device
  * error word and the kernel exits.  jst_device_error() synchronises the
  * current device and returns (and clears) that word: 0 = none, 1 = timeout.
+ * It covers every entry point of this library, jst_gemm_tc_noalloc included.
  */
 int jst_device_error(void);
+
+/*
+ * Testing aid (no counterpart in the reference): set an error word of the
+ * current device from the host, exactly as a kernel whose bounded wait gave
+ * up would, so that a caller's handling of jst_device_error() can be tested
+ * without stalling or faulting a GPU.  word 0: the word of the allocating
+ * entry points; word 1: the word of jst_gemm_tc_noalloc.  JST_ERR_ARG for
+ * any other value.
+ */
+int jst_test_set_device_error(int word);
 
 /* Release cached device workspace and pinned staging buffers of this process
  * (including the jst_copy_h2d / jst_copy_d2h staging chunks). */

@@ -94,6 +94,8 @@ def load() -> ctypes.CDLL:
     lib.jst_copy_d2h.argtypes = [vp, vp, ctypes.c_size_t, vp]
     lib.jst_device_error.restype = ci
     lib.jst_device_error.argtypes = []
+    lib.jst_test_set_device_error.restype = ci
+    lib.jst_test_set_device_error.argtypes = [ci]
     lib.jst_release_caches.restype = None
     lib.jst_release_caches.argtypes = []
     lib.jst_launch_count.restype = ctypes.c_int64

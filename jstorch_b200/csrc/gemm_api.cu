@@ -470,15 +470,41 @@ int jst_matmul_host_async(const float* a, const float* b, float* c, int M, int K
 
 int jst_device_error(void) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || !jst::g_dev[dev].err_word) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
         cudaGetLastError();
         return 0;
     }
     cudaDeviceSynchronize();
     uint32_t e = 0;
-    cudaMemcpy(&e, jst::g_dev[dev].err_word, sizeof(e), cudaMemcpyDeviceToHost);
-    if (e) cudaMemset(jst::g_dev[dev].err_word, 0, sizeof(uint32_t));
-    return (int)e;
+    if (jst::g_dev[dev].err_word) {
+        cudaMemcpy(&e, jst::g_dev[dev].err_word, sizeof(e), cudaMemcpyDeviceToHost);
+        if (e) cudaMemset(jst::g_dev[dev].err_word, 0, sizeof(uint32_t));
+    }
+    uint32_t en = 0;  // jst_gemm_tc_noalloc keeps its own word
+    jst::noalloc_take_error(dev, &en);
+    cudaGetLastError();
+    return (int)(e | en);
+}
+
+int jst_test_set_device_error(int word) {
+    int dev = 0;
+    if (word == 0) {
+        int rc = jst::current_device(&dev);
+        if (rc) return rc;
+        const uint32_t one = 1;
+        if (cudaMemcpy(jst::g_dev[dev].err_word, &one, sizeof(one), cudaMemcpyHostToDevice) != cudaSuccess) {
+            cudaGetLastError();
+            return jst::set_status(JST_ERR_CUDA, "writing the device error word failed");
+        }
+        return jst::set_status(JST_OK, nullptr);
+    }
+    if (word != 1) return jst::set_status(JST_ERR_ARG, "jst_test_set_device_error: word must be 0 or 1");
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return jst::set_status(JST_ERR_NO_DEVICE, "no CUDA device available");
+    }
+    const int rc = jst::noalloc_set_error(dev, 1);
+    return rc ? rc : jst::set_status(JST_OK, nullptr);
 }
 
 void jst_release_caches(void) {

@@ -63,6 +63,11 @@ int set_status(int status, const char* msg);
 
 // Per-device error word written by kernels whose bounded waits gave up.
 uint32_t* device_error_word();
+// The separate timeout word of jst_gemm_tc_noalloc (a file-scope device
+// variable, so that entry point allocates nothing): read-and-clear on device
+// `dev` (0 when that entry point never ran there), and a host-side setter.
+int noalloc_take_error(int dev, uint32_t* out);
+int noalloc_set_error(int dev, uint32_t value);
 
 // 3 x TF32 tcgen05 path
 size_t tc_workspace_bytes(const GemmArgs& a);

@@ -687,27 +687,40 @@ int tc_gemm_run(const GemmArgs& a, void* workspace, cudaStream_t s) {
 // ----------------------------------------------------------------------------
 // Allocation-free variant (jst_gemm_tc_noalloc).
 //
-// Some callers cannot call cudaMalloc at all: code running while a CUDA graph
-// is being captured (an allocation there is either illegal or baked into the
-// graph), processes whose device memory is owned by another allocator that
-// forbids side allocations, and embedders that must size all device memory up
-// front.  For them the split planes of the 3xTF32 kernel live in this fixed,
+// Some callers cannot call cudaMalloc: hosts whose device memory is owned by
+// another allocator that forbids side allocations (an embedding runtime that
+// hands the library a fixed arena), embedders that must size all device
+// memory up front, and latency-critical code that cannot afford cudaMalloc /
+// cudaFree, which may synchronise the whole device.  For them the split
+// planes (and split-K partials) of the 3xTF32 kernel live in this fixed,
 // file-scope device array instead of a workspace from the library's pool.
 //
 // The array is NOALLOC_SCRATCH_BYTES (64 MiB) and belongs to this module: the
 // CUDA runtime reserves it on a device when the module is loaded there (on
 // first use with lazy module loading, which is the default; at context
 // creation with CUDA_MODULE_LOADING=EAGER), and it is held until the process
-// exits.  A request whose split planes, 2 * Kp * (M + N) * batch floats with
-// Kp = K rounded up to 4, exceed it is rejected with JST_ERR_ARG.
+// exits.  The real limit is what tc_workspace_bytes() returns for the request:
+//   2 * Kp * (M * Ba + N * Bb) * 4 bytes of hi / lo planes (Kp = K rounded up
+//   to 4; Ba, Bb = batch, or 1 for an operand with batch stride 0; Ba = 0
+//   when A is split inside the kernel, which narrow tiles of a K-major A do)
+//   + S * batch * M * N * 4 bytes of split-K partials (S > 1 only when the
+//   output tiles fill less than half the SMs).
+// A request above 64 MiB is rejected with JST_ERR_ARG before any device work.
 //
 // The array is shared by every call on a device and keeps the previous call's
 // planes.  Nothing in it has to start at zero: the split kernels rewrite every
-// row and every padded column of the planes a call uses before the GEMM reads
-// them.  The kernel's timeout word is also file-scope; each call zeroes it on
-// its stream before launching.  Two calls whose work overlaps on the GPU (on
-// different streams, or from different threads) race on the array and give
-// wrong results: serialise them.
+// row and every padded column of the planes a call uses, and every split-K
+// partial is written before the reduce reads it.  Two calls whose work
+// overlaps on the GPU (on different streams, or from different threads) race
+// on the array and give wrong results: serialise them.
+//
+// The kernel's timeout word is file-scope too.  It starts at zero when the
+// module loads, a kernel whose bounded wait gave up ORs its flag into it, and
+// jst_device_error() reads and clears it together with the word of the
+// allocating entry points -- so a timed-out call is reported the same way on
+// both paths.  The device addresses of both arrays are looked up once per
+// device and cached; cudaDeviceReset() (which unloads the module) is not
+// supported in a process that has called this entry point.
 // ----------------------------------------------------------------------------
 constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(64) << 20;
 static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_SCRATCH_BYTES / sizeof(float)];
@@ -749,6 +762,41 @@ int noalloc_setup(int dev, NoAllocDevice** out) {
 }
 }  // namespace
 
+// The noalloc timeout word of device `dev`: *out = its value (0 when the
+// entry point never ran there), then cleared.  Called by jst_device_error()
+// after it has synchronised the device.
+int noalloc_take_error(int dev, uint32_t* out) {
+    *out = 0;
+    if (dev < 0 || dev >= 64) return JST_OK;
+    uint32_t* w = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (g_noalloc_dev[dev].ready) w = g_noalloc_dev[dev].err;
+    }
+    if (!w) return JST_OK;
+    if (cudaMemcpy(out, w, sizeof(uint32_t), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return set_status(JST_ERR_CUDA, "reading the scratch error word failed");
+    }
+    if (*out && cudaMemset(w, 0, sizeof(uint32_t)) != cudaSuccess) {
+        cudaGetLastError();
+        return set_status(JST_ERR_CUDA, "clearing the scratch error word failed");
+    }
+    return JST_OK;
+}
+
+// Host-side stand-in for a timed-out noalloc kernel (jst_test_set_device_error).
+int noalloc_set_error(int dev, uint32_t value) {
+    NoAllocDevice* nd = nullptr;
+    int rc = noalloc_setup(dev, &nd);
+    if (rc) return rc;
+    if (cudaMemcpy(nd->err, &value, sizeof(value), cudaMemcpyHostToDevice) != cudaSuccess) {
+        cudaGetLastError();
+        return set_status(JST_ERR_CUDA, "writing the scratch error word failed");
+    }
+    return JST_OK;
+}
+
 }  // namespace jst
 
 extern "C" int jst_gemm_tc_noalloc(const jst_gemm_desc* d) {
@@ -782,10 +830,8 @@ extern "C" int jst_gemm_tc_noalloc(const jst_gemm_desc* d) {
     NoAllocDevice* nd = nullptr;
     rc = noalloc_setup(dev, &nd);
     if (rc) return rc;
-    if (cudaMemsetAsync(nd->err, 0, sizeof(uint32_t), s) != cudaSuccess) {
-        cudaGetLastError();
-        return set_status(JST_ERR_CUDA, "clearing the scratch error word failed");
-    }
+    // the timeout word is not cleared here: a flag left by an earlier call
+    // stays set until jst_device_error() reads it
     rc = tc_gemm_launch(a, nd->scratch, nd->err, s);
     return rc ? rc : set_status(JST_OK, nullptr);
 }

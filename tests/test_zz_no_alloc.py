@@ -1,11 +1,16 @@
-"""jst_gemm_tc_noalloc: the tensor-core GEMM for callers that cannot allocate
-device memory (graph capture, foreign allocators, fixed memory budgets).  It
-keeps its scratch in a fixed 64 MiB device array instead of allocating.
+"""jst_gemm_tc_noalloc: the tensor-core GEMM for callers that cannot call
+cudaMalloc (a host whose device memory belongs to another allocator, an
+embedder with a fixed memory budget, latency-critical code that cannot afford
+the device-wide synchronisation cudaMalloc / cudaFree may cause).  It keeps its
+scratch in a fixed 64 MiB device array instead of allocating.
 
 Checked through the C ABI against jst_gemm_ex (the allocating entry point,
 tensor-core kernel forced) on two calls in a row with different shapes and
-inputs, so the second call runs on scratch the first one left behind.  This
-file is collected last on purpose; it also passes when run on its own.
+inputs, so the second call runs on scratch the first one left behind; on a
+shape that splits K (the partials live in the same array); with the device's
+free memory unchanged across calls; and with a timed-out wait (raised from
+the host) reported by jst_device_error().  This file is collected last on
+purpose; it also passes when run on its own.
 """
 import ctypes
 
@@ -92,3 +97,53 @@ def test_noalloc_rejects_requests_beyond_the_fixed_scratch():
     _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d)))
     torch.cuda.synchronize()
     assert float(c.abs().max()) == 0.0
+
+
+def test_noalloc_split_k_shape_matches_oracle():
+    # 2 output tiles and K = 8192: the kernel splits K into slices whose
+    # partials also live in the fixed scratch
+    _run_pair(256, 256, 8192, seed=3)
+    _run_pair(256, 256, 8192, seed=4, with_bias=True, relu=True)
+
+
+def test_noalloc_calls_leave_free_device_memory_unchanged():
+    import torch
+    lib = _lib.load()
+    rng = np.random.default_rng(5)
+    M, N, K = 512, 768, 1536
+    a = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
+    b = torch.from_numpy(rng.standard_normal((K, N), dtype=np.float32)).cuda()
+    c = torch.empty((M, N), device="cuda")
+    d = _desc(a, b, c, M, N, K, stream=torch.cuda.current_stream().cuda_stream)
+    _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d)))  # the module (and its array) is resident from here
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(2):
+        _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d)))
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    assert free1 == free0, (free0, free1)
+    ref = oracle.gemm_f64(a.cpu().numpy(), b.cpu().numpy())
+    err, where = oracle.max_rel_err(a.cpu().numpy(), b.cpu().numpy(), c.cpu().numpy(), ref)
+    assert err <= TOL, (err, where)
+
+
+def test_noalloc_timeout_word_is_reported_by_device_error():
+    # A kernel whose bounded wait gives up ORs a flag into the entry point's
+    # own error word; the flag is planted from the host here (no GPU stall).
+    import torch
+    lib = _lib.load()
+    a = torch.ones((128, 256), device="cuda")
+    b = torch.ones((256, 128), device="cuda")
+    c = torch.empty((128, 128), device="cuda")
+    d = _desc(a, b, c, 128, 128, 256, stream=torch.cuda.current_stream().cuda_stream)
+    _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d)))
+    assert lib.jst_device_error() == 0
+    _lib.check(lib.jst_test_set_device_error(1))
+    # a later call does not wipe the flag before the caller has seen it
+    _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d)))
+    assert lib.jst_device_error() == 1
+    assert lib.jst_device_error() == 0  # read and cleared
+    torch.cuda.synchronize()
+    assert float(c.min()) == 256.0 and float(c.max()) == 256.0
+    assert lib.jst_test_set_device_error(2) == 1  # JST_ERR_ARG
