@@ -121,6 +121,12 @@ def load() -> ctypes.CDLL:
         getattr(lib, name).argtypes = [vp] * 4 + [ci] * 16 + [vp]
     lib.jst_gru_layer_forward.restype = ci
     lib.jst_gru_layer_forward.argtypes = [vp, ci, ci, ci, ci, vp, vp, vp, vp, vp, ci, vp, ctypes.c_int64, vp, vp]
+    lib.jst_gru_layer_forward_train.restype = ci
+    lib.jst_gru_layer_forward_train.argtypes = [vp, ci, ci, ci, ci, vp, vp, vp, vp, vp, ci, vp, ctypes.c_int64, vp,
+                                                vp, vp]
+    lib.jst_gru_layer_backward.restype = ci
+    lib.jst_gru_layer_backward.argtypes = ([vp, ci, ci, ci, ci, vp, vp, vp, ci, vp, ctypes.c_int64, vp, vp,
+                                            ctypes.c_int64, vp] + [vp] * 6 + [ci, vp])
     _lib = lib
     return lib
 

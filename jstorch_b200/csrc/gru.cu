@@ -41,9 +41,12 @@ constexpr int kMaxSlices = 16;  // K-slices of the recurrent GEMM (recurrent_sli
 
 // h_out[b][j] from gi[b][{j, H+j, 2H+j}], gh[b][...] (or b_hh when gh is
 // null) and h_prev[b][j] (or 0 when null).
+// saved (training forward, else null): [batch][4H] rows of r, z, n and the
+// n-gate's recurrent term gh_n, which the backward pass reads.
 __global__ void gru_gate_kernel(const float* __restrict__ gi, const float* __restrict__ gh,
                                 const float* __restrict__ b_hh, const float* __restrict__ h_prev, int64_t ld_prev,
-                                float* __restrict__ h_out, int64_t ld_out, int batch, int H) {
+                                float* __restrict__ h_out, int64_t ld_out, int batch, int H,
+                                float* __restrict__ saved) {
     const int64_t total = (int64_t)batch * H;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(i / H), j = (int)(i - (int64_t)b * H);
@@ -65,6 +68,13 @@ __global__ void gru_gate_kernel(const float* __restrict__ gi, const float* __res
         const float h = h_prev ? h_prev[(int64_t)b * ld_prev + j] : 0.0f;
         const float one_minus_z = __fadd_rn(-z, 1.0f);
         h_out[(int64_t)b * ld_out + j] = __fadd_rn(__fmul_rn(one_minus_z, n), __fmul_rn(z, h));
+        if (saved) {
+            float* sv = saved + (int64_t)b * 4 * H;
+            sv[j] = r;
+            sv[H + j] = z;
+            sv[2 * H + j] = n;
+            sv[3 * H + j] = ghn;
+        }
     }
 }
 
@@ -81,7 +91,8 @@ __global__ void __launch_bounds__(256) gru_gate_t_kernel(const float* __restrict
                                                          int slices, const float* __restrict__ b_hh,
                                                          const float* __restrict__ h_prev, int64_t ld_prev,
                                                          float* __restrict__ h_out, int64_t ld_out, int batch, int H,
-                                                         float* __restrict__ nh_hi, float* __restrict__ nh_lo, int Kp) {
+                                                         float* __restrict__ nh_hi, float* __restrict__ nh_lo, int Kp,
+                                                         float* __restrict__ saved) {
     __shared__ float g[3][8][33];  // [gate][hidden unit][batch row]
     ptx::griddep_wait();  // launched as a programmatic dependent of the step's GEMM
     const int j0 = blockIdx.x * 8, b0 = blockIdx.y * 32;
@@ -123,6 +134,13 @@ __global__ void __launch_bounds__(256) gru_gate_t_kernel(const float* __restrict
     const float one_minus_z = __fadd_rn(-z, 1.0f);
     const float hv = __fadd_rn(__fmul_rn(one_minus_z, n), __fmul_rn(z, h));
     h_out[(int64_t)b * ld_out + j] = hv;
+    if (saved) {
+        float* sv = saved + (int64_t)b * 4 * H;
+        sv[j] = r;
+        sv[H + j] = z;
+        sv[2 * H + j] = n;
+        sv[3 * H + j] = g[2][jl][bl];
+    }
     if (nh_hi) {
         const float hi = ptx::to_tf32(hv);
         nh_hi[(int64_t)b * Kp + j] = hi;
@@ -130,13 +148,139 @@ __global__ void __launch_bounds__(256) gru_gate_t_kernel(const float* __restrict
     }
 }
 
+// ------------------------------------------------------------------ backward
+// One step of back-propagation through time for the cell of nn.js:477-485,
+// the gradients GradTensor's closures produce for its ops (sigmoid, tanh,
+// mul, add, slice; native/core/autograd.hpp) composed for one (b, j):
+//   g   = dL/dh'  = dout_t + (z' g')_next + (dgh_next . W_hh)
+//   dn  = g (1 - z)        dz = g (h - n)        dh_direct = g z
+//   da_n = dn (1 - n^2)    da_r = (da_n gh_n) r (1 - r)    da_z = dz z (1 - z)
+//   dgi = (da_r, da_z, da_n)        dgh = (da_r, da_z, da_n r)
+// `part` holds S slices of P = dgh_next . W_hh with element (b, j) of slice
+// sl at part[sl * plane + j * sj + b * sb] (the tensor-core path's [H][batch]
+// partials, or one [batch][H] product), or is null at the first backward
+// step.  A block takes 8 hidden units x 32 batch rows: it sums the slices in
+// order with batch fastest (128-byte reads of the [H][batch] partials),
+// transposes through shared memory, then works with 8 threads along the
+// hidden units per batch row (whole 32-byte sectors of the [batch][..] rows).
+// With p_hi set it also writes the tf32 hi / lo split of dgh into the
+// [batch][Kp3] planes the next step's GEMM reads.
+__global__ void __launch_bounds__(256) gru_gate_bwd_kernel(
+    const float* __restrict__ part, int slices, int64_t plane, int64_t sj, int64_t sb,
+    const float* __restrict__ carry_in, const float* __restrict__ dout, int64_t ld_dout,
+    const float* __restrict__ saved, const float* __restrict__ h_prev, int64_t ld_prev, float* __restrict__ dgi,
+    float* __restrict__ dgh, float* __restrict__ carry_out, float* __restrict__ p_hi, float* __restrict__ p_lo,
+    int Kp3, int batch, int H) {
+    __shared__ float ps[8][33];  // [hidden unit][batch row]
+    ptx::griddep_wait();  // a programmatic dependent of the step's GEMM
+    const int j0 = blockIdx.x * 8, b0 = blockIdx.y * 32;
+    const int t = threadIdx.x;
+    {
+        const int bl = t & 31, jl = t >> 5;  // sum phase: batch fastest
+        const int j = j0 + jl, b = b0 + bl;
+        float acc = 0.0f;
+        if (part && j < H && b < batch) {
+            float v[kMaxSlices];
+#pragma unroll
+            for (int sl = 0; sl < kMaxSlices; ++sl) v[sl] = sl < slices ? part[sl * plane + j * sj + b * sb] : 0.0f;
+#pragma unroll
+            for (int sl = 0; sl < kMaxSlices; ++sl)
+                if (sl < slices) acc += v[sl];
+        }
+        ps[jl][bl] = acc;
+    }
+    __syncthreads();
+    const int jl = t & 7, bl = t >> 3;  // gate phase: hidden unit fastest
+    const int j = j0 + jl, b = b0 + bl;
+    if (b >= batch || j >= H) return;
+    float g = ps[jl][bl];
+    if (carry_in) g = __fadd_rn(g, carry_in[(int64_t)b * H + j]);
+    if (dout) g = __fadd_rn(g, dout[(int64_t)b * ld_dout + j]);
+    const float* sv = saved + (int64_t)b * 4 * H;
+    const float r = sv[j], z = sv[H + j], n = sv[2 * H + j], ghn = sv[3 * H + j];
+    const float hp = h_prev ? h_prev[(int64_t)b * ld_prev + j] : 0.0f;
+    const float dn = __fmul_rn(g, __fadd_rn(1.0f, -z));
+    const float dz = __fmul_rn(g, __fadd_rn(hp, -n));
+    const float dan = __fmul_rn(dn, __fadd_rn(1.0f, -__fmul_rn(n, n)));
+    const float dar = __fmul_rn(__fmul_rn(dan, ghn), __fmul_rn(r, __fadd_rn(1.0f, -r)));
+    const float daz = __fmul_rn(dz, __fmul_rn(z, __fadd_rn(1.0f, -z)));
+    const float dghn = __fmul_rn(dan, r);
+    float* gi_row = dgi + (int64_t)b * 3 * H;
+    float* gh_row = dgh + (int64_t)b * 3 * H;
+    gi_row[j] = dar;
+    gi_row[H + j] = daz;
+    gi_row[2 * H + j] = dan;
+    gh_row[j] = dar;
+    gh_row[H + j] = daz;
+    gh_row[2 * H + j] = dghn;
+    carry_out[(int64_t)b * H + j] = __fmul_rn(g, z);
+    if (p_hi) {
+        float* hi = p_hi + (int64_t)b * Kp3;
+        float* lo = p_lo + (int64_t)b * Kp3;
+        const float v3[3] = {dar, daz, dghn};
+#pragma unroll
+        for (int gate = 0; gate < 3; ++gate) {
+            const float h = ptx::to_tf32(v3[gate]);
+            hi[gate * H + j] = h;
+            lo[gate * H + j] = ptx::to_tf32(v3[gate] - h);
+        }
+    }
+}
+
+// dh0 = carry (z_0 g_0) + P (the S slices of dgh_0 . W_hh, layout as above);
+// accumulate adds it to dh0's contents.
+__global__ void gru_dh0_kernel(const float* __restrict__ part, int slices, int64_t plane, int64_t sj, int64_t sb,
+                               const float* __restrict__ carry, float* __restrict__ dh0, int accumulate, int batch,
+                               int H) {
+    ptx::griddep_wait();
+    const int64_t total = (int64_t)batch * H;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(i / H), j = (int)(i - (int64_t)b * H);
+        float acc = 0.0f;
+        for (int sl = 0; sl < slices; ++sl) acc += part[sl * plane + j * sj + b * sb];
+        float v = __fadd_rn(acc, carry[i]);
+        if (accumulate) v = __fadd_rn(dh0[i], v);
+        dh0[i] = v;
+    }
+}
+
+// Column sums of a [rows][cols] matrix in a fixed order (bit-identical
+// reruns): pass 1 sums row chunks into partial[chunk][cols], pass 2 adds the
+// chunks in order (and to out's contents when accumulating).
+constexpr int kColsumRows = 256;
+__global__ void colsum_partial_kernel(const float* __restrict__ a, int64_t rows, int cols,
+                                      float* __restrict__ partial) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= cols) return;
+    const int64_t r0 = (int64_t)blockIdx.y * kColsumRows;
+    const int64_t r1 = std::min<int64_t>(r0 + kColsumRows, rows);
+    float acc = 0.0f;
+    for (int64_t r = r0; r < r1; ++r) acc += a[r * cols + j];
+    partial[(int64_t)blockIdx.y * cols + j] = acc;
+}
+
+__global__ void colsum_final_kernel(const float* __restrict__ partial, int nchunks, int cols, float* __restrict__ out,
+                                    int accumulate) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= cols) return;
+    float acc = 0.0f;
+    for (int c = 0; c < nchunks; ++c) acc += partial[(int64_t)c * cols + j];
+    out[j] = accumulate ? __fadd_rn(out[j], acc) : acc;
+}
+
+// dst += src (n floats)
+__global__ void accumulate_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        dst[i] = __fadd_rn(dst[i], src[i]);
+}
+
 int gate(const float* gi, const float* gh, const float* b_hh, const float* h_prev, int64_t ld_prev, float* h_out,
-         int64_t ld_out, int batch, int H, cudaStream_t s) {
+         int64_t ld_out, int batch, int H, float* saved, cudaStream_t s) {
     const int64_t total = (int64_t)batch * H;
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
     {
         ProfScope prof(s, KID_RNN);
-        gru_gate_kernel<<<blocks, 256, 0, s>>>(gi, gh, b_hh, h_prev, ld_prev, h_out, ld_out, batch, H);
+        gru_gate_kernel<<<blocks, 256, 0, s>>>(gi, gh, b_hh, h_prev, ld_prev, h_out, ld_out, batch, H, saved);
     }
     return cudaPeekAtLastError() == cudaSuccess ? JST_OK : set_status(JST_ERR_CUDA, "gru gate launch failed");
 }
@@ -161,27 +305,32 @@ bool use_tc_recurrent(int batch, int H) {
     return H >= 128 && batch >= 8 && (double)3 * H * H * batch >= (double)(1 << 24);
 }
 
-// K-slices for ghT = W_hh . h^T (M = 3H, N = batch): fill the SMs with
-// (tile, slice) CTAs, slices of at least 4 BK steps; normalised so that no
-// slice is empty.
-int recurrent_slices(int batch, int H) {
-    const int bn = tc_pick_bn(3 * H, batch, H);
-    const int tiles = ((3 * H + 127) / 128) * ((batch + bn - 1) / bn);
-    const int num_kb = (H + 15) / 16;
-    int S = std::min(std::min(148 / std::max(tiles, 1), num_kb / 4), 16);
+// K-slices of a recurrent product with few output tiles (M x N, reduction K):
+// fill the SMs with (tile, slice) CTAs, slices of at least 4 BK steps;
+// normalised so that no slice is empty.  Forward: ghT = W_hh . h^T (M = 3H,
+// N = batch, K = H); backward: P^T = W_hh^T . dgh^T (M = H, N = batch, K = 3H).
+int product_slices(int M, int N, int K) {
+    const int bn = tc_pick_bn(M, N, K);
+    const int tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+    const int num_kb = (K + 15) / 16;
+    int S = std::min(std::min(148 / std::max(tiles, 1), num_kb / 4), kMaxSlices);
     if (S <= 1) return 1;
     const int per = (num_kb + S - 1) / S;
     return (num_kb + per - 1) / per;
 }
 
+int recurrent_slices(int batch, int H) { return product_slices(3 * H, batch, H); }
+
 }  // namespace
 }  // namespace jst
 
-extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int input_size, int hidden,
-                                     const float* w_ih, const float* w_hh, const float* b_ih, const float* b_hh,
-                                     const float* h0, int reverse, float* out, int64_t ld_out, float* h_n,
-                                     jst_stream_t stream) {
-    using namespace jst;
+namespace jst {
+namespace {
+// One layer and direction forward; `saved` (null for inference) receives
+// [seq][batch][4H] rows of r, z, n, gh_n for the backward pass.
+int gru_forward_impl(const float* x, int seq, int batch, int input_size, int hidden, const float* w_ih,
+                     const float* w_hh, const float* b_ih, const float* b_hh, const float* h0, int reverse, float* out,
+                     int64_t ld_out, float* h_n, float* saved, jst_stream_t stream) {
     if (seq < 0 || batch < 0 || input_size < 0 || hidden < 0)
         return set_status(JST_ERR_ARG, "gru: negative size");
     if (ld_out < hidden) return set_status(JST_ERR_ARG, "gru: ld_out < hidden");
@@ -244,7 +393,8 @@ extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int inp
                     // scheduled while the GEMM drains and wait for it in-kernel
                     if (launch_dependent(gru_gate_t_kernel, dim3((hidden + 7) / 8, (batch + 31) / 32), dim3(256), 0, s,
                                          git, (const float*)part, S, b_hh, h_prev, ld_prev, h_out, ld_out, batch,
-                                         hidden, more ? h_hi : nullptr, more ? h_lo : nullptr, Kp) != cudaSuccess)
+                                         hidden, more ? h_hi : nullptr, more ? h_lo : nullptr, Kp,
+                                         saved ? saved + (int64_t)t * batch * 4 * hidden : nullptr) != cudaSuccess)
                         rc = set_status(JST_ERR_CUDA, "gru gate launch failed");
                     h_split = more;
                 }
@@ -258,7 +408,8 @@ extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int inp
                 if (rc) break;
                 ghp = gh;
             }
-            rc = gate(git, ghp, b_hh, h_prev, ld_prev, h_out, ld_out, batch, hidden, s);
+            rc = gate(git, ghp, b_hh, h_prev, ld_prev, h_out, ld_out, batch, hidden,
+                      saved ? saved + (int64_t)t * batch * 4 * hidden : nullptr, s);
         }
         h_prev = h_out;
         ld_prev = ld_out;
@@ -271,4 +422,236 @@ extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int inp
     const int frc = workspace_free(ws, s);
     if (rc) return rc;
     return frc ? frc : set_status(JST_OK, nullptr);
+}
+}  // namespace
+}  // namespace jst
+
+extern "C" int jst_gru_layer_forward(const float* x, int seq, int batch, int input_size, int hidden,
+                                     const float* w_ih, const float* w_hh, const float* b_ih, const float* b_hh,
+                                     const float* h0, int reverse, float* out, int64_t ld_out, float* h_n,
+                                     jst_stream_t stream) {
+    return jst::gru_forward_impl(x, seq, batch, input_size, hidden, w_ih, w_hh, b_ih, b_hh, h0, reverse, out, ld_out,
+                                 h_n, nullptr, stream);
+}
+
+extern "C" int jst_gru_layer_forward_train(const float* x, int seq, int batch, int input_size, int hidden,
+                                           const float* w_ih, const float* w_hh, const float* b_ih, const float* b_hh,
+                                           const float* h0, int reverse, float* out, int64_t ld_out, float* h_n,
+                                           float* saved, jst_stream_t stream) {
+    if (!saved && seq > 0 && batch > 0 && hidden > 0) return jst::set_status(JST_ERR_ARG, "gru: null saved buffer");
+    return jst::gru_forward_impl(x, seq, batch, input_size, hidden, w_ih, w_hh, b_ih, b_hh, h0, reverse, out, ld_out,
+                                 h_n, saved, stream);
+}
+
+namespace jst {
+namespace {
+
+int launch_ok(const char* what) {
+    return cudaPeekAtLastError() == cudaSuccess ? JST_OK : set_status(JST_ERR_CUDA, what);
+}
+
+// Column sums of a [rows][cols] row-major matrix into out (added when accumulating).
+int colsum(const float* a, int64_t rows, int cols, float* partial, float* out, int accumulate, cudaStream_t s) {
+    const int nchunks = (int)((rows + kColsumRows - 1) / kColsumRows);
+    {
+        ProfScope prof(s, KID_RNN);
+        colsum_partial_kernel<<<dim3((cols + 255) / 256, nchunks), 256, 0, s>>>(a, rows, cols, partial);
+    }
+    {
+        ProfScope prof(s, KID_RNN);
+        colsum_final_kernel<<<(cols + 255) / 256, 256, 0, s>>>(partial, nchunks, cols, out, accumulate);
+    }
+    return launch_ok("gru: column-sum launch failed");
+}
+
+// Run the GEMM `d` into dst (n floats, packed); when accumulating, into tmp
+// first and then added to dst's contents.
+int gemm_into(jst_gemm_desc d, float* dst, int64_t n, int accumulate, float* tmp, cudaStream_t s) {
+    d.C = accumulate ? tmp : dst;
+    int rc = jst_gemm_ex(&d);
+    if (rc || !accumulate) return rc;
+    {
+        ProfScope prof(s, KID_RNN);
+        const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
+        accumulate_kernel<<<blocks, 256, 0, s>>>(dst, tmp, n);
+    }
+    return launch_ok("gru: accumulate launch failed");
+}
+
+int gru_backward_impl(const float* x, int seq, int batch, int input_size, int hidden, const float* w_ih,
+                      const float* w_hh, const float* h0, int reverse, const float* out, int64_t ld_out,
+                      const float* saved, const float* dout, int64_t ld_dout, const float* dh_n, float* dx,
+                      float* dw_ih, float* dw_hh, float* db_ih, float* db_hh, float* dh0, int accumulate,
+                      cudaStream_t s) {
+    const int H = hidden;
+    const int64_t rows = (int64_t)seq * batch, G = 3LL * H;
+    const bool tc = use_tc_recurrent(batch, H);
+    const int Kp3 = (int)((G + 3) & ~3LL);
+    const int S = tc ? product_slices(H, batch, (int)G) : 1;
+    auto up = [](size_t n) { return (n + 63) & ~size_t(63); };
+    const size_t n_g = up((size_t)rows * G), n_hp = up((size_t)rows * H), n_c = up((size_t)batch * H);
+    const size_t n_p = up(tc ? (size_t)S * H * batch : (size_t)batch * H);
+    const size_t n_wt = tc ? up((size_t)H * Kp3) : 0, n_pl = tc ? up((size_t)batch * Kp3) : 0;
+    const size_t n_cs = up((size_t)((rows + kColsumRows - 1) / kColsumRows) * G);
+    const int acc_dx = (accumulate & JST_GRU_ACC_DX) != 0, acc_p = (accumulate & JST_GRU_ACC_PARAMS) != 0,
+              acc_h = (accumulate & JST_GRU_ACC_DH0) != 0;
+    const size_t n_tmp =
+        (acc_dx || acc_p) ? up(std::max<size_t>((size_t)rows * input_size, (size_t)G * std::max(input_size, H))) : 0;
+    void* ws = nullptr;
+    int rc = workspace_alloc((2 * n_g + n_hp + 2 * n_c + n_p + 2 * n_wt + 2 * n_pl + n_cs + n_tmp) * sizeof(float), s,
+                             &ws);
+    if (rc) return rc;
+    float* dgi = static_cast<float*>(ws);  // [seq][batch][3H]
+    float* dgh = dgi + n_g;                // [seq][batch][3H]
+    float* hp = dgh + n_g;                 // [seq][batch][H]: the state each step started from
+    float* carry[2] = {hp + n_hp, hp + n_hp + n_c};
+    float* P = carry[1] + n_c;
+    float* wt_hi = P + n_p;
+    float* wt_lo = wt_hi + n_wt;
+    float* p_hi = wt_lo + n_wt;
+    float* p_lo = p_hi + n_pl;
+    float* cs_part = p_lo + n_pl;
+    float* tmp = cs_part + n_cs;
+    auto cuda_ok = [&](cudaError_t e, const char* what) -> int {
+        if (e == cudaSuccess) return JST_OK;
+        cudaGetLastError();
+        return set_status(JST_ERR_CUDA, what);
+    };
+    // hp: step t started from out[t -/+ 1] (forward / reverse), the first
+    // step processed from h0 (zeros when null)
+    const int64_t blk = (int64_t)batch * H;
+    const int t_first = reverse ? seq - 1 : 0;
+    if (seq > 1)
+        rc = cuda_ok(cudaMemcpy2DAsync(hp + (reverse ? 0 : blk), (size_t)H * 4, out + (reverse ? batch * ld_out : 0),
+                                       (size_t)ld_out * 4, (size_t)H * 4, (size_t)(seq - 1) * batch,
+                                       cudaMemcpyDeviceToDevice, s),
+                     "gru: state copy");
+    if (!rc)
+        rc = h0 ? cuda_ok(cudaMemcpyAsync(hp + t_first * blk, h0, (size_t)blk * 4, cudaMemcpyDeviceToDevice, s),
+                          "gru: h0 copy")
+                : cuda_ok(cudaMemsetAsync(hp + t_first * blk, 0, (size_t)blk * 4, s), "gru: zero state");
+    // W_hh^T as the A operand of P^T = W_hh^T . dgh^T, split once
+    if (!rc && tc) rc = tc_split(w_hh, 0, H, 0, H, (int)G, 1, wt_hi, wt_lo, s);
+    // the partials' layout: [S][H][batch] (tensor cores) or [batch][H] (one product)
+    const int64_t plane = tc ? (int64_t)H * batch : blk, sj = tc ? batch : 1, sb = tc ? 1 : H;
+    for (int step = seq - 1; step >= 0 && !rc; --step) {  // processing order, last step first
+        const int t = reverse ? seq - 1 - step : step;
+        const bool first = step == seq - 1;
+        const bool need_product = step > 0 || dh0 != nullptr;
+        float* dgh_t = dgh + (int64_t)t * batch * G;
+        {
+            ProfScope prof(s, KID_RNN);
+            if (launch_dependent(gru_gate_bwd_kernel, dim3((H + 7) / 8, (batch + 31) / 32), dim3(256), 0, s,
+                                 first ? (const float*)nullptr : (const float*)P, first ? 0 : S, plane, sj, sb,
+                                 first ? dh_n : (const float*)carry[(step + 1) & 1],
+                                 dout ? dout + (int64_t)t * batch * ld_dout : nullptr, ld_dout,
+                                 saved + (int64_t)t * batch * 4 * H, (const float*)(hp + t * blk), (int64_t)H,
+                                 dgi + (int64_t)t * batch * G, dgh_t, carry[step & 1],
+                                 tc && need_product ? p_hi : nullptr, p_lo, Kp3, batch, H) != cudaSuccess)
+                rc = set_status(JST_ERR_CUDA, "gru: backward gate launch failed");
+        }
+        if (!rc) rc = launch_ok("gru: backward gate launch failed");
+        if (rc || !need_product) break;
+        // P = dgh_t . W_hh (nn.js:481's matmul, backward: g . b^T with b = W_hh^T)
+        if (tc) {
+            rc = tc_gemm_planes(wt_hi, wt_lo, p_hi, p_lo, H, batch, (int)G, 1, P, batch, (int64_t)H * batch, nullptr,
+                                0, device_error_word(), s, 0, nullptr, 0, 0, 0, 0, 0, S, 0, 0, 0, /*pdl=*/1);
+        } else {
+            jst_gemm_desc d;
+            jst_gemm_desc_init(&d, batch, H, (int)G, dgh_t, w_hh, P);
+            d.stream = reinterpret_cast<jst_stream_t>(s);
+            rc = jst_gemm_ex(&d);
+        }
+    }
+    if (!rc && dh0) {
+        ProfScope prof(s, KID_RNN);
+        const int blocks = (int)std::min<int64_t>((blk + 255) / 256, 148 * 8);
+        if (launch_dependent(gru_dh0_kernel, dim3(blocks), dim3(256), 0, s, (const float*)P, S, plane, sj, sb,
+                             (const float*)carry[0], dh0, acc_h, batch, H) != cudaSuccess)
+            rc = set_status(JST_ERR_CUDA, "gru: dh0 launch failed");
+    }
+    if (!rc) rc = launch_ok("gru: dh0 launch failed");
+    auto desc = [&](int M, int N, int K) {
+        jst_gemm_desc d;
+        jst_gemm_desc_init(&d, M, N, K, nullptr, nullptr, nullptr);
+        d.stream = reinterpret_cast<jst_stream_t>(s);
+        return d;
+    };
+    // dW_ih = dGI^T . X (all steps at once: one TN GEMM with K = seq * batch)
+    if (!rc && dw_ih) {
+        jst_gemm_desc d = desc((int)G, input_size, (int)rows);
+        d.transA = 1; d.A = dgi; d.lda = G;
+        d.B = x; d.ldb = input_size;
+        rc = gemm_into(d, dw_ih, G * input_size, acc_p, tmp, s);
+    }
+    // dW_hh = dGH^T . Hprev
+    if (!rc && dw_hh) {
+        jst_gemm_desc d = desc((int)G, H, (int)rows);
+        d.transA = 1; d.A = dgh; d.lda = G;
+        d.B = hp; d.ldb = H;
+        rc = gemm_into(d, dw_hh, G * H, acc_p, tmp, s);
+    }
+    if (!rc && db_ih) rc = colsum(dgi, rows, (int)G, cs_part, db_ih, acc_p, s);
+    if (!rc && db_hh) rc = colsum(dgh, rows, (int)G, cs_part, db_hh, acc_p, s);
+    // dX = dGI . W_ih
+    if (!rc && dx) {
+        jst_gemm_desc d = desc((int)rows, input_size, (int)G);
+        d.A = dgi; d.lda = G;
+        d.B = w_ih; d.ldb = input_size;
+        rc = gemm_into(d, dx, rows * input_size, acc_dx, tmp, s);
+    }
+    const int frc = workspace_free(ws, s);
+    if (rc) return rc;
+    return frc ? frc : set_status(JST_OK, nullptr);
+}
+
+}  // namespace
+}  // namespace jst
+
+extern "C" int jst_gru_layer_backward(const float* x, int seq, int batch, int input_size, int hidden,
+                                      const float* w_ih, const float* w_hh, const float* h0, int reverse,
+                                      const float* out, int64_t ld_out, const float* saved, const float* dout,
+                                      int64_t ld_dout, const float* dh_n, float* dx, float* dw_ih, float* dw_hh,
+                                      float* db_ih, float* db_hh, float* dh0, int accumulate, jst_stream_t stream) {
+    using namespace jst;
+    if (seq < 0 || batch < 0 || input_size < 0 || hidden < 0)
+        return set_status(JST_ERR_ARG, "gru backward: negative size");
+    if (accumulate & ~(JST_GRU_ACC_DX | JST_GRU_ACC_PARAMS | JST_GRU_ACC_DH0))
+        return set_status(JST_ERR_ARG, "gru backward: unknown accumulate flag");
+    const int64_t rows = (int64_t)seq * batch, G = 3LL * hidden;
+    if (rows > 0x7fffffffLL || G > 0x7fffffffLL) return set_status(JST_ERR_ARG, "gru backward: size exceeds int");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (hidden == 0) return set_status(JST_OK, nullptr);
+    if (seq == 0 || batch == 0) {  // no step: parameter gradients are zero, dh0 = dh_n
+        if (!(accumulate & JST_GRU_ACC_PARAMS)) {
+            const struct { float* p; size_t n; } z[] = {{dw_ih, (size_t)G * input_size}, {dw_hh, (size_t)G * hidden},
+                                                        {db_ih, (size_t)G}, {db_hh, (size_t)G}};
+            for (const auto& e : z)
+                if (e.p && cudaMemsetAsync(e.p, 0, e.n * 4, s) != cudaSuccess) {
+                    cudaGetLastError();
+                    return set_status(JST_ERR_CUDA, "gru backward: zero fill");
+                }
+        }
+        if (dh0 && batch) {
+            const size_t n = (size_t)batch * hidden * 4;
+            cudaError_t e = cudaSuccess;
+            if (!(accumulate & JST_GRU_ACC_DH0)) e = dh_n ? cudaMemcpyAsync(dh0, dh_n, n, cudaMemcpyDeviceToDevice, s)
+                                      : cudaMemsetAsync(dh0, 0, n, s);
+            else if (dh_n) {
+                ProfScope prof(s, KID_RNN);
+                accumulate_kernel<<<148, 256, 0, s>>>(dh0, dh_n, (int64_t)batch * hidden);
+                e = cudaPeekAtLastError();
+            }
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                return set_status(JST_ERR_CUDA, "gru backward: dh0");
+            }
+        }
+        return set_status(JST_OK, nullptr);
+    }
+    if (ld_out < hidden || (dout && ld_dout < hidden)) return set_status(JST_ERR_ARG, "gru backward: leading dimension < hidden");
+    if (!w_hh || !out || !saved) return set_status(JST_ERR_ARG, "gru backward: null w_hh, out or saved");
+    if ((dx && !w_ih) || (dw_ih && !x)) return set_status(JST_ERR_ARG, "gru backward: null w_ih or x");
+    return gru_backward_impl(x, seq, batch, input_size, hidden, w_ih, w_hh, h0, reverse, out, ld_out, saved, dout,
+                             ld_dout, dh_n, dx, dw_ih, dw_hh, db_ih, db_hh, dh0, accumulate, s);
 }

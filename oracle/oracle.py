@@ -12,6 +12,7 @@ product (jstorch_b200) never calls it.
   conv2d_backward_weight_f64 /             convolution launchers (1-D = 2-D
   conv_transpose2d_backward_weight_f64     with H = 1), tap by tap
   gru_forward_f64                          fp64 restatement of the reference's GRU
+  gru_backward_f64                         its gradients (what GradTensor computes)
 
 Reference citations are relative to the JsTorch project root.
 """
@@ -354,3 +355,91 @@ def gru_forward_f64(x, params, hidden, num_layers=1, bidirectional=False, h0=Non
             hn.append(h)
         inp = np.concatenate(outs, axis=2)
     return inp, np.stack(hn)
+
+
+def gru_backward_f64(x, params, hidden, num_layers=1, bidirectional=False, h0=None, dout=None, dh_n=None):
+    """Gradients of the reference GRU (src/nn.js:451-536) in fp64, for the loss
+    L = sum(dout * output) + sum(dh_n * h_n), batch_first = False.
+
+    What the reference's GradTensor computes when the GRU's parameters require
+    grad (nn.js:442-444): its backward sweep (native/core/autograd.hpp:40-65)
+    through the cell's two matmuls ({g . b^T, a^T . g}, autograd.hpp:433-441,
+    with b = W^T so dW = g^T . a), the bias adds (unbroadcast = sum over the
+    batch, autograd.hpp:324-342), the slices, sigmoid (s' = s (1 - s)), tanh
+    (t' = 1 - t^2), the products and the (1 - z) term, composed per step:
+        g = dL/dh' ;  dn = g (1 - z) ;  dz = g (h - n) ;  dh = g z + dgh . W_hh
+        da_n = dn (1 - n^2) ; da_r = da_n gh_n r (1 - r) ; da_z = dz z (1 - z)
+        dgi = (da_r, da_z, da_n) ;  dgh = (da_r, da_z, da_n r)
+    Returns (grads {param name: fp64 array}, dx [seq, batch, in], dh0 [layers*dirs,
+    batch, H] or None)."""
+    x = np.asarray(x, np.float64)
+    seq, batch = x.shape[0], x.shape[1]
+    H = hidden
+    sig = lambda v: 1.0 / (1.0 + np.exp(-v))
+    dirs = 2 if bidirectional else 1
+    # forward, keeping every step's gate values and the state it started from
+    inps, tapes = [], []
+    inp = x
+    for l in range(num_layers):
+        outs, tl = [], []
+        for d in range(dirs):
+            sfx = "_reverse" if d else ""
+            wih = np.asarray(params[f"weight_ih_l{l}{sfx}"], np.float64)
+            whh = np.asarray(params[f"weight_hh_l{l}{sfx}"], np.float64)
+            bih = np.asarray(params[f"bias_ih_l{l}{sfx}"], np.float64)
+            bhh = np.asarray(params[f"bias_hh_l{l}{sfx}"], np.float64)
+            h = np.zeros((batch, H)) if h0 is None else np.asarray(h0[l * dirs + d], np.float64)
+            out = np.zeros((seq, batch, H))
+            tape = {}
+            for t in (range(seq - 1, -1, -1) if d else range(seq)):
+                gi = inp[t] @ wih.T + bih
+                gh = h @ whh.T + bhh
+                r = sig(gi[:, :H] + gh[:, :H])
+                z = sig(gi[:, H:2 * H] + gh[:, H:2 * H])
+                n = np.tanh(gi[:, 2 * H:] + r * gh[:, 2 * H:])
+                tape[t] = (r, z, n, gh[:, 2 * H:], h)
+                h = (1 - z) * n + z * h
+                out[t] = h
+            outs.append(out)
+            tl.append(tape)
+        inps.append(inp)
+        tapes.append(tl)
+        inp = np.concatenate(outs, axis=2)
+    # backward, last layer first
+    g_out = np.zeros((seq, batch, H * dirs)) if dout is None else np.asarray(dout, np.float64)
+    grads = {}
+    dh0 = np.zeros((num_layers * dirs, batch, H)) if h0 is not None else None
+    for l in range(num_layers - 1, -1, -1):
+        inp = inps[l]
+        dinp = np.zeros_like(inp)
+        for d in range(dirs):
+            sfx = "_reverse" if d else ""
+            wih = np.asarray(params[f"weight_ih_l{l}{sfx}"], np.float64)
+            whh = np.asarray(params[f"weight_hh_l{l}{sfx}"], np.float64)
+            gw_ih, gw_hh = np.zeros_like(wih), np.zeros_like(whh)
+            gb_ih, gb_hh = np.zeros(3 * H), np.zeros(3 * H)
+            dh = np.zeros((batch, H)) if dh_n is None else np.asarray(dh_n[l * dirs + d], np.float64).copy()
+            for t in (range(seq) if d else range(seq - 1, -1, -1)):
+                r, z, n, ghn, hp = tapes[l][d][t]
+                gt = dh + g_out[t, :, d * H:(d + 1) * H]
+                dn = gt * (1 - z)
+                dz = gt * (hp - n)
+                dan = dn * (1 - n * n)
+                dar = dan * ghn * r * (1 - r)
+                daz = dz * z * (1 - z)
+                dgi = np.concatenate([dar, daz, dan], axis=1)
+                dgh = np.concatenate([dar, daz, dan * r], axis=1)
+                gw_ih += dgi.T @ inp[t]
+                gw_hh += dgh.T @ hp
+                gb_ih += dgi.sum(0)
+                gb_hh += dgh.sum(0)
+                dinp[t] += dgi @ wih
+                dh = gt * z + dgh @ whh
+            if dh0 is not None:
+                dh0[l * dirs + d] = dh
+            grads[f"weight_ih_l{l}{sfx}"] = gw_ih
+            grads[f"weight_hh_l{l}{sfx}"] = gw_hh
+            grads[f"bias_ih_l{l}{sfx}"] = gb_ih
+            grads[f"bias_hh_l{l}{sfx}"] = gb_hh
+        g_out = dinp
+    return grads, g_out, dh0

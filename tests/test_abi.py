@@ -114,9 +114,18 @@ def test_no_device_is_an_error_not_a_fallback():
 
 def test_rnn_header_exported_and_validates_without_gpu():
     names = _lib.header_functions(_lib.RNN_HEADER)
-    assert names == ["jst_gru_layer_forward"]
+    assert names == ["jst_gru_layer_backward", "jst_gru_layer_forward", "jst_gru_layer_forward_train"]
     lib = _lib.load()
-    assert hasattr(lib, "jst_gru_layer_forward")
+    for n in names:
+        assert hasattr(lib, n)
     # ld_out < hidden and a negative size are rejected on the host
     assert lib.jst_gru_layer_forward(16, 2, 2, 4, 8, 16, 16, None, None, None, 0, 16, 4, None, None) == 1
     assert lib.jst_gru_layer_forward(16, -1, 2, 4, 8, 16, 16, None, None, None, 0, 16, 8, None, None) == 1
+    # training entry points: a null saved buffer, an unknown accumulate bit
+    # and a negative size are rejected on the host
+    assert lib.jst_gru_layer_forward_train(16, 2, 2, 4, 8, 16, 16, None, None, None, 0, 16, 8, None, None,
+                                           None) == 1
+    bw = lambda acc, seq=2: lib.jst_gru_layer_backward(16, seq, 2, 4, 8, 16, 16, None, 0, 16, 8, 16, 16, 8, None,
+                                                       None, None, None, None, None, None, acc, None)
+    assert bw(8) == 1
+    assert bw(0, seq=-1) == 1
