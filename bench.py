@@ -133,17 +133,22 @@ class ClockSampler:
                 "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
-def _traffic_from_profiles() -> tuple[float | None, str | None]:
-    """DRAM bytes per tc_gemm launch at 8192^3 from the committed ncu summary
-    (its `dram_bytes_per_launch:` line)."""
-    p = ROOT / "profiles" / "tc_gemm_8192_dram.md"
-    if not p.exists():
-        return None, None
-    for line in p.read_text().splitlines():
-        if line.strip().startswith("dram_bytes_per_launch:"):
-            return float(line.split(":", 1)[1].strip()), "ncu dram__bytes_read.sum + dram__bytes_write.sum, " \
-                "one capture of a bench tc_gemm launch at 8192^3 (profiles/tc_gemm_8192_dram.md)"
-    return None, None
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one tc_gemm
+# launch at 8192^3, from a one-pass ncu capture of this bench's own launches:
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none
+#       -k regex:tc_gemm -s 6 -c 1 python bench.py --steps 2 --warmup 3
+#       --no-e2e --no-cpu-baseline --no-ref-gpu
+# It is not measured by the run that prints it; the line says so.
+TC_GEMM_8192_DRAM_BYTES = 4.82545e9
+
+
+def workload(world: int) -> str:
+    """config.workload of both arms (this library and the reference's CPU
+    path) at `world` GPUs, so the driver can match the two lines."""
+    if world == 1:
+        return "config3: C=A.B, M=N=K=8192, A,B~N(0,1), row-major fp32"
+    return (f"config5 row-sharded: C=A.B, M={SIZE * world} ({SIZE} rows per rank), K=N={SIZE}, "
+            f"A,B~U[-1,1), row-major fp32")
 
 
 def cpu_baseline(A: np.ndarray, B: np.ndarray, target_s: float = 12.0) -> dict:
@@ -170,44 +175,53 @@ def cpu_baseline(A: np.ndarray, B: np.ndarray, target_s: float = 12.0) -> dict:
 
 
 def run_reference(args) -> None:
+    """The reference's CPU path (fp32 i-k-j loop in its row-major layout, all
+    host threads) on this arm's workload at args.gpus GPUs.  Each step is a
+    bounded sample of rows of C; ms_per_step is the measured time of that
+    sample, and the rate extrapolates linearly to the full product."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from jstorch_b200 import synth
     from oracle import oracle
 
-    A, B = synth.config3()
-    M, K = A.shape
-    N = B.shape[1]
-    C = np.zeros((M, N), np.float32)
-    # size one step to ~4 s of CPU work
+    world = args.gpus
+    if world == 1:
+        A, B = synth.config3()
+        M = SIZE
+    else:  # rows of config 5 (the sample never needs the whole 65536-row A)
+        M = SIZE * world
+        A, B = synth.config5(rows=2048)
+    K, N = A.shape[1], B.shape[1]
+    C = np.zeros((A.shape[0], N), np.float32)
+    # size one step so that warm-up + steps stay within about a minute
     t0 = time.perf_counter()
     threads = oracle.sgemm_f32_cpu(A, B, C, 0, 8)
-    rate = 8 / max(time.perf_counter() - t0, 1e-6)
-    rows = int(max(8, min(M, rate * 4.0)))
-    for w in range(args.warmup):
+    rate = 8 / max(time.perf_counter() - t0, 1e-6)  # rows per second
+    per_step_s = min(4.0, max(0.3, 45.0 / max(args.steps, 1)))
+    rows = int(max(8, min(A.shape[0], rate * per_step_s)))
+    for _ in range(args.warmup):
         oracle.sgemm_f32_cpu(A, B, C, 0, min(rows, 8))
     times = []
     for s in range(args.steps):
-        r0 = (s * rows) % max(M - rows + 1, 1)
+        r0 = (s * rows) % max(A.shape[0] - rows + 1, 1)
         t0 = time.perf_counter()
         oracle.sgemm_f32_cpu(A, B, C, r0, rows)
         times.append(time.perf_counter() - t0)
     total = sum(times)
-    flops = 2.0 * rows * N * K * args.steps
-    tflops = flops / total / 1e12
-    ms_full = 2.0 * M * N * K / (tflops * 1e12) * 1e3
+    tflops = 2.0 * rows * N * K * args.steps / total / 1e12
+    sample = (f"{rows} rows of C per step ({rows}x{N}x{K}), {args.steps} steps, fp32 i-k-j loop in the reference's "
+              f"row-major layout (the reference has no CPU path of its own)")
     line = {
         "impl": "reference", "metric": "fp32 GEMM TFLOP/s at 8192^3", "value": tflops, "unit": "TFLOP/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_full,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total / args.steps * 1e3,
+        "ms_full_product_extrapolated": 2.0 * M * N * K / (tflops * 1e12) * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (numpy PCG64, seed 2)",
-        "config": {"workload": "config3: C=A.B, M=N=K=8192, A,B~N(0,1), row-major fp32",
-                   "sample_per_step": f"{rows} rows of C", "parallelism": "host threads"},
-        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": f"{rows} rows of C per step ({rows}x{N}x{K}), {args.steps} steps, "
-                                   f"fp32 i-k-j loop (the reference has no CPU path; this is its row-major "
-                                   f"fp32 loop)"},
+        "data": f"synthetic (numpy PCG64, seed {2 if world == 1 else 4})",
+        "config": {"workload": workload(world), "sample_per_step": f"{rows} rows of C",
+                   "parallelism": f"{threads} host threads"},
+        "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -269,11 +283,41 @@ def _ref_gpu_library(args, a, b, c, stream, flops) -> dict:
         torch.backends.cuda.matmul.allow_tf32 = False
 
 
+TOL = 2e-6  # max |C - C_ref| / (||A_i,:|| ||B_:,j||) against the fp64 product
+REST_S = 1.5  # pause before a measured pass: lets the power cap's budget recover
+
+
+def _sample_rows(world: int, m_local: int, chunk: int, per_rank: int) -> list[int]:
+    """Global rows of C to check: `per_rank` rows of every rank's blocks,
+    spread over its blocks, at seeded offsets inside each block."""
+    from jstorch_b200 import dist as jdist
+
+    rng = np.random.default_rng(12345)
+    rows = []
+    for r in range(world):
+        plan = jdist.row_plan(world, r, m_local, chunk)
+        for j in range(per_rank):
+            blk = plan[(j * len(plan)) // per_rank]
+            rows.append(blk.global_row0 + int(rng.integers(blk.rows)))
+    return sorted(rows)
+
+
+def _allreduce_max(values: list[float]) -> list[float]:
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(values, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t]
+
+
 def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     """N > 1: configuration 5's row-sharded GEMM with 8192 rows of A per rank
     (M = 8192 N, K = N = 8192, A, B ~ U[-1, 1), seed 4).  One step = B
-    broadcast from rank 0 + every rank's GEMM + the all-gather of C, through
-    jst_gemm_rowsharded; device-timed per rank, max over ranks."""
+    broadcast from rank 0 + every rank's GEMM + the delivery of C to every
+    rank, through jst_gemm_rowsharded; device-timed per rank, max over ranks.
+    After the timed loop every rank checks sampled rows of every rank's blocks
+    of its own C against the fp64 oracle; the run fails if any is off."""
     import datetime
 
     import torch
@@ -282,6 +326,7 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     from jstorch_b200 import _lib
     from jstorch_b200 import dist as jdist
     from jstorch_b200 import synth
+    from oracle import oracle
 
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))  # host plumbing only
     dev = torch.device("cuda", local)
@@ -289,9 +334,11 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     chunk = args.chunk_rows
     M = m_local * world
     plan = jdist.row_plan(world, rank, m_local, chunk)
-    a_host = np.concatenate([synth.config5(rows=blk.rows, row0=blk.global_row0)[0] for blk in plan])
-    b_host = synth.config5(rows=1)[1] if rank == 0 else np.zeros((K, N), np.float32)
+    a_host = np.concatenate([synth.matrix(4, synth.A, blk.rows, K, "uniform", row0=blk.global_row0)
+                             for blk in plan])
+    b_host = synth.matrix(4, synth.B, K, N, "uniform") if rank == 0 else np.zeros((K, N), np.float32)
     comm = jdist.Comm.from_process_group(timeout_s=120.0)
+    comm_nranks = int(jdist.load().jst_comm_size(comm.handle))
     a = torch.from_numpy(a_host).to(dev)
     b = torch.from_numpy(b_host).to(dev)
     # how C reaches every rank (--c-gather):
@@ -330,7 +377,6 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     comm.sync(stream)
     dist.barrier()
     n0 = _lib.launch_count()
-    _lib.profile_enable(True)
     clocks = ClockSampler(local) if rank == 0 else None
     if clocks:
         clocks.start()
@@ -352,8 +398,6 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     dist.barrier()
     clk = clocks.stop() if clocks else None
     launches = _lib.launch_count() - n0
-    kstats = _lib.profile_read()
-    _lib.profile_enable(False)
     ms_local = ev0.elapsed_time(ev1) / args.steps
     t = torch.tensor([ms_local, float(launches)], dtype=torch.float64)
     tmax = t.clone()
@@ -362,6 +406,29 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
     ms = float(tmax[0])
     value = flops / (ms * 1e-3) / 1e12
+
+    # ---- parity: sampled rows of every rank's blocks, read from this rank's C
+    # (the product of the last timed step), against the fp64 oracle
+    per_rank = 8 if world <= 4 else 4
+    rows = _sample_rows(world, m_local, chunk, per_rank)
+    b_full = synth.matrix(4, synth.B, K, N, "uniform")
+    a_rows = np.concatenate([synth.matrix(4, synth.A, 1, K, "uniform", row0=g) for g in rows])
+    got = c[torch.tensor(rows, device=dev)].cpu().numpy()
+    err_local, where = oracle.max_rel_err(a_rows, b_full, got, oracle.gemm_f64(a_rows, b_full))
+    b_ok = float(np.array_equal(b.cpu().numpy(), b_full))  # B arrived in place on every rank
+    err_max, b_bad = _allreduce_max([err_local, 1.0 - b_ok])
+    parity = {"max_rel_err": err_max, "tol": TOL, "ok": bool(err_max <= TOL and b_bad == 0.0),
+              "rows_checked_per_rank": len(rows), "ranks_checked": world,
+              "what": f"{per_rank} seeded rows of every rank's blocks, read from each rank's own C after the timed "
+                      f"steps, vs fp64 oracle; B compared bit for bit on every rank"}
+
+    # ---- per-kernel device times: one extra step with events around each launch
+    _lib.profile_enable(True)
+    step()
+    comm.sync(stream)
+    kstats = _lib.profile_read()
+    _lib.profile_enable(False)
+    dist.barrier()
 
     timeline = None
     if args.trace:  # one extra step with the library's event timeline (not timed)
@@ -419,17 +486,19 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
                 "peak_note": f"3xTF32 roofline = {peak_kind} / 2 / 3; rank 0's launches ({chunk}-row blocks, two "
                              f"compute streams, so per-launch times overlap)",
                 "kernel_ms": kernel_ms,
+                "kernel_timing": "CUDA events around each launch on its stream, one step after the timed loop",
                 "kernels": {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in kstats.items()}}
     line = {
         "metric": "fp32 GEMM TFLOP/s at 8192^3", "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (numpy PCG64, seed 4)",
-        "config": {"workload": f"config5 row-sharded: C=A.B, M={M} (8192 rows per rank), K=N=8192, "
-                               f"A,B~U[-1,1); B broadcast (NCCL), C gathered on every rank, {chunk}-row blocks",
-                   "c_gather": gather,
+        "config": {"workload": workload(world),
+                   "c_gather": gather, "b": "broadcast in place from rank 0 (NCCL)",
+                   "chunk_rows": chunk,
                    "parallelism": f"row-sharded x{world}",
                    "l2": "inputs larger than L2 (A shard, B 256 MiB each per rank)"},
+        "parity": parity, "nccl_comm_nranks": comm_nranks,
         "e2e": e2e, "roofline": roofline, "gpu_launches": int(tsum[1]), "clocks": clk,
     }
     if timeline:
@@ -443,6 +512,106 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     if rank == 0:
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
+    if not parity["ok"]:
+        raise SystemExit(f"rank {rank}: sharded product failed its check (max rel err {err_max:.3e}, "
+                         f"local worst at {where}, B mismatch {b_bad})")
+
+
+def run_config4_sharded(args, rank: int, world: int, local: int) -> None:
+    """Configuration 4 with the batch index sharded over N GPUs: the scores
+    GEMM (64 x [512x64].[64x512]) then the output GEMM (64 x [512x512].[512x64]),
+    each through jst_bmm_batchsharded (rank r computes batches
+    [r*64/N, (r+1)*64/N) into place, then an in-place all-gather of C).
+    Total work is fixed as N grows ("scaling": "strong").  Every rank checks
+    two batches of every rank's share of both outputs against the fp64 oracle."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from jstorch_b200 import _lib
+    from jstorch_b200 import dist as jdist
+    from jstorch_b200 import synth
+    from oracle import oracle
+
+    if 64 % world:
+        raise SystemExit("config 4 shards 64 batches: N must divide 64")
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    dev = torch.device("cuda", local)
+    q, kt, p_, v = synth.config4()
+    bl = 64 // world
+    mine = slice(rank * bl, (rank + 1) * bl)
+    tq, tk, tp, tv = (torch.from_numpy(np.ascontiguousarray(x[mine])).to(dev) for x in (q, kt, p_, v))
+    s_full = torch.empty((64, 512, 512), device=dev)
+    o_full = torch.empty((64, 512, 64), device=dev)
+    comm = jdist.Comm.from_process_group(timeout_s=120.0)
+    comm_nranks = int(jdist.load().jst_comm_size(comm.handle))
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    flops = 2 * (2.0 * 64 * 512 * 512 * 64)
+
+    def step():
+        comm.bmm_batchsharded(tq, tk, s_full, stream=stream)
+        comm.bmm_batchsharded(tp, tv, o_full, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    comm.sync(stream)
+    dist.barrier()
+    n0 = _lib.launch_count()
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    if clocks:
+        clocks.mark_start()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    comm.sync(stream)
+    if clocks:
+        clocks.mark_end()
+    dist.barrier()
+    clk = clocks.stop() if clocks else None
+    launches = _lib.launch_count() - n0
+    ms, _ = _allreduce_max([ev0.elapsed_time(ev1) / args.steps, 0.0])
+    t = torch.tensor([float(launches)], dtype=torch.float64)
+    dist.all_reduce(t)
+    value = flops / (ms * 1e-3) / 1e12
+
+    # parity: two batches of every rank's share, both products, on every rank
+    batches = sorted({r * bl + j for r in range(world) for j in (0, bl - 1)})
+    s_got, o_got = s_full[batches].cpu().numpy(), o_full[batches].cpu().numpy()
+    qs, ks, ps, vs = q[batches], kt[batches], p_[batches], v[batches]
+    e1, _ = oracle.max_rel_err(qs, ks, s_got, oracle.gemm_f64(qs, ks))
+    e2, _ = oracle.max_rel_err(ps, vs, o_got, oracle.gemm_f64(ps, vs))
+    err_max, _ = _allreduce_max([max(e1, e2), 0.0])
+    parity = {"max_rel_err": err_max, "tol": TOL, "ok": bool(err_max <= TOL),
+              "what": f"batches {batches} of both outputs, read from each rank's own C, vs fp64 oracle"}
+    # compulsory bytes of the two products: q, kt, S and p, v, O, fp32
+    nbytes = 4.0 * 64 * (512 * 64 + 64 * 512 + 512 * 512 + 512 * 512 + 512 * 64 + 512 * 64)
+    line = {
+        "metric": "config4 strided-batched attention shapes, batch-sharded", "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (numpy PCG64, seed 3)",
+        "config": {"workload": "config4: batch 64 of [512x64].[64x512] then batch 64 of [512x512].[512x64], "
+                               "N(0,1/8)", "parallelism": f"batch-sharded x{world} ({bl} batches per rank), "
+                                                          f"C all-gathered in place (NCCL)"},
+        "compulsory_bytes_per_step": nbytes,
+        "parity": parity, "nccl_comm_nranks": comm_nranks, "gpu_launches": int(t[0]), "clocks": clk,
+    }
+    comm.destroy()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.destroy_process_group()
+    if not parity["ok"]:
+        raise SystemExit(f"rank {rank}: batch-sharded product failed its check (max rel err {err_max:.3e})")
 
 
 def _time_device(fn, steps: int, warmup: int, stream) -> float:
@@ -747,6 +916,48 @@ def run_config(args) -> None:
                     "context": {"reference_design_tf32_ms": refd, "cudnn_fp32_ms": cudnn},
                     "note": "context rows: the reference's per-step JS op sequence restated with torch "
                             "(TF32 on, as matmul.cu:12); torch.nn.GRU (cuDNN) with TF32 off"})
+    elif args.config == 9:
+        # GRU training step (nn.js:442-444 under GradTensor): forward_train + backward of the
+        # config-8 model, loss = sum(dout * output), through jst_gru_layer_forward_train /
+        # jst_gru_layer_backward
+        from jstorch_b200.rnn import GRU
+
+        seq, batch, inp, H, layers = 64, 64, 512, 1024, 2
+        gen = torch.Generator(device=dev).manual_seed(9)
+        gru = GRU(inp, H, layers, generator=gen)
+        x = torch.randn((seq, batch, inp), device=dev, generator=gen)
+        dout = torch.randn((seq, batch, H), device=dev, generator=gen)
+        fwd_flops = sum(2.0 * seq * batch * 3 * H * ((inp if l == 0 else H) + H) for l in range(layers))
+        flops = 3.0 * fwd_flops  # backward: dgh.W_hh, dW_hh, dW_ih and dX, each the size of a forward product
+
+        def train_step():
+            out_, hn, ctx = gru.forward_train(x)
+            gru.backward(ctx, dout)
+
+        gru.backward(gru.forward_train(x)[2], dout)
+        ms = _time_device(train_step, args.steps, args.warmup, stream)
+        _lib.profile_enable(True)  # per-kernel breakdown from a separate, event-bracketed pass
+        _time_device(train_step, 1, 1, stream)
+        ks = _lib.profile_read()
+        _lib.profile_enable(False)
+        torch.backends.cudnn.allow_tf32 = False
+        torch.backends.cuda.matmul.allow_tf32 = False
+        tg = torch.nn.GRU(inp, H, layers).to(dev)
+        xr = x.clone().requires_grad_(True)
+
+        def cudnn_step():
+            o, _ = tg(xr)
+            o.backward(dout)
+
+        cudnn = _time_device(cudnn_step, args.steps, args.warmup, stream)
+        tf = lambda t: flops / (t * 1e-3) / 1e12
+        out.update({"metric": "GRU training step (forward + backward), seq 64, batch 64, 512->1024, 2 layers",
+                    "unit": "ms", "value": ms, "higher_is_better": False, "tflops": tf(ms),
+                    "kernels": {k: {"launches": v[0], "ms": v[1]} for k, v in ks.items()},
+                    "kernels_note": "one step, from an event-bracketed pass outside the timed one",
+                    "context": {"cudnn_fp32_ms": cudnn, "cudnn_fp32_tflops": tf(cudnn)},
+                    "note": "loss = sum(dout * output); all parameter gradients and dx computed; context row: "
+                            "torch.nn.GRU (cuDNN) forward + backward with TF32 off"})
     print(json.dumps(out), flush=True)
 
 
@@ -779,15 +990,14 @@ def run_jstorch(args) -> None:
     torch.cuda.set_stream(stream)  # every library call below runs on this stream
     flops = 2.0 * M * N * K
 
-    # ---- device-resident timing (value) + live kernel timing (roofline)
+    # ---- device-resident timing (value): plain launches, no per-launch events
     for _ in range(args.warmup):
         jstorch_b200.gemm(a, b, out=c, kernel=args.kernel)
     torch.cuda.synchronize()
     n0 = _lib.launch_count()
-    _lib.profile_enable(True)
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.3)
+    time.sleep(REST_S)  # the timed burst starts with the power budget recovered (see the sustained leg)
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -800,12 +1010,61 @@ def run_jstorch(args) -> None:
     clocks.mark_end()
     clk = clocks.stop()
     launches = _lib.launch_count() - n0
-    kstats = _lib.profile_read()
-    _lib.profile_enable(False)
     ms = ev0.elapsed_time(ev1) / args.steps
     value = flops / (ms * 1e-3) / 1e12
     if jstorch_b200.device_error():
         raise SystemExit("device error word set during the benchmark")
+
+    # ---- per-kernel device times (roofline): a separate pass of the same
+    # calls, each launch bracketed by CUDA events on the stream it is
+    # launched on (the events keep a GEMM from starting under its split's
+    # tail, so this pass is not the timed one).  The B200's 1 kW power cap
+    # pulls the SM clock down after ~0.1 s of this kernel at full clock, so
+    # the pass starts after a pause, like the timed loop and like the burst
+    # peak it is compared with; its clocks are sampled too.
+    prof_steps = max(3, min(args.steps, 10))
+    time.sleep(REST_S)
+    pclocks = ClockSampler(local)
+    pclocks.start()
+    time.sleep(0.3)
+    pclocks.mark_start()
+    _lib.profile_enable(True)
+    for _ in range(prof_steps):
+        jstorch_b200.gemm(a, b, out=c, kernel=args.kernel)
+    torch.cuda.synchronize()
+    pclocks.mark_end()
+    kstats = _lib.profile_read()
+    _lib.profile_enable(False)
+    pclk = pclocks.stop()
+
+    # ---- the same call under sustained load (seconds of back-to-back GEMMs,
+    # the regime of a long job: power-capped clocks), against the sustained peak
+    sustained = None
+    if not args.no_sustained and M == SIZE:
+        time.sleep(REST_S)
+        sclocks = ClockSampler(local)
+        sclocks.start()
+        time.sleep(0.3)
+        n_s = 250
+        for _ in range(50):  # reach the capped steady state first
+            jstorch_b200.gemm(a, b, out=c, kernel=args.kernel)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        sclocks.mark_start()
+        e0.record(stream)
+        for _ in range(n_s):
+            jstorch_b200.gemm(a, b, out=c, kernel=args.kernel)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        sclocks.mark_end()
+        sclk = sclocks.stop()
+        s_ms = e0.elapsed_time(e1) / n_s
+        s_tf = flops / (s_ms * 1e-3) / 1e12
+        s_peak = (_peaks().get("bf16_tflops_sustained") or 0.0) / 6.0
+        sustained = {"ms_per_step": s_ms, "value": s_tf, "steps": n_s, "clocks": sclk,
+                     "peak": s_peak or None, "frac": (s_tf / s_peak) if s_peak else None,
+                     "note": "whole call (splits + GEMM) after 50 untimed calls, against the sustained 3xTF32 "
+                             "roofline (dense bf16 sustained / 6)"}
 
     # ---- end to end through the host-array entry point (pinned host buffers)
     e2e = None
@@ -820,14 +1079,20 @@ def run_jstorch(args) -> None:
     name, (nl, tot) = top
     kernel_ms = tot / max(nl, 1)
     achieved = flops / (kernel_ms * 1e-3) / 1e12 if kernel_ms > 0 else None
-    traffic, traffic_src = _traffic_from_profiles()
+    full_size = M == SIZE and args.kernel in ("auto", "tc3xtf32")
     roofline = {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
                 "frac_of_burst": (achieved / burst) if achieved else None,
-                "traffic": traffic,
+                "traffic": TC_GEMM_8192_DRAM_BYTES if full_size else None,
+                "traffic_source": ("one ncu capture of a bench tc_gemm launch at 8192^3 with the command in "
+                                   "bench.py (not measured by this run)") if full_size else None,
+                "algorithmic_bytes": 4.0 * (2 * (M + N) * ((K + 3) // 4 * 4) + M * N),
                 "peak_note": f"3xTF32 roofline = {peak_kind} / 2 (TF32 rate) / 3 (three products)",
-                "traffic_note": traffic_src,
                 "kernel_ms": kernel_ms,
+                "kernel_timing": f"CUDA events around each launch on its stream, {prof_steps} calls after a "
+                                 f"{REST_S} s pause (clocks: {pclk.get('sm_mhz')} MHz median, "
+                                 f"reasons {pclk.get('reasons')})",
+                "kernel_clocks": pclk,
                 "kernels": {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in kstats.items()}}
 
     # ---- reference GPU library path (cuBLAS sgemm with TF32 math, as the
@@ -839,10 +1104,11 @@ def run_jstorch(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (numpy PCG64, seed 2)",
-        "config": {"workload": f"config3: C=A.B, M=N=K={M}, A,B~N(0,1), row-major fp32, device-resident",
-                   "kernel": args.kernel, "parallelism": "single GPU",
+        "config": {"workload": workload(1) if M == SIZE else f"config3 leading block: C=A.B, M=N=K={M}",
+                   "residency": "A, B, C device-resident", "kernel": args.kernel, "parallelism": "single GPU",
                    "l2": "inputs larger than L2 (A, B, C 256 MiB each; split planes 1 GiB)"},
         "e2e": e2e, "roofline": roofline, "gpu_launches": launches, "clocks": clk,
+        "sustained": sustained,
         "reference_gpu_library": ref_gpu,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -861,8 +1127,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-ref-gpu", action="store_true")
+    ap.add_argument("--no-sustained", action="store_true", help="N=1: skip the sustained-load figure")
     ap.add_argument("--size", type=int, default=SIZE, help="square GEMM size at N=1 (default 8192)")
-    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5, 6, 7, 8],
+    ap.add_argument("--config", type=int, default=0, choices=[0, 1, 2, 3, 4, 5, 6, 7, 8, 9],
                     help="secondary measurement of one BASELINE configuration (0: the headline line)")
     ap.add_argument("--trace", action="store_true", help="N>1: add one traced step's timeline to the line")
     ap.add_argument("--c-gather", choices=["auto", "multicast", "copy", "nccl"], default="auto",
@@ -873,8 +1140,15 @@ def main() -> None:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == 4 and world > 1:
+        import torch
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        run_config4_sharded(args, int(os.environ.get("RANK", "0")), world, local)
     elif args.config:
         run_config(args)
     else:

@@ -217,7 +217,14 @@ int jst_comm_trace_read(jst_comm* c, char* labels, double* ms, int max_entries) 
 }
 
 int jst_comm_rank(const jst_comm* c) { return c ? c->rank : -1; }
-int jst_comm_size(const jst_comm* c) { return c ? c->nranks : -1; }
+// The rank count NCCL reports for the communicator (the requested count once
+// the communicator is gone).
+int jst_comm_size(const jst_comm* c) {
+    if (!c) return -1;
+    int n = c->nranks;
+    if (c->nccl && !c->broken && ncclCommCount(c->nccl, &n) != ncclSuccess) n = c->nranks;
+    return n;
+}
 
 int jst_comm_destroy(jst_comm* c) {
     using namespace jst;

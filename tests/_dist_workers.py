@@ -54,6 +54,37 @@ def gloo_rowsharded_layout(rank: int, world: int, port: int, out_q) -> None:
         out_q.put((rank, traceback.format_exc()))
 
 
+def gloo_batchsharded_layout(rank: int, world: int, port: int, out_q) -> None:
+    """Host logic of jst_bmm_batchsharded on CPU ranks: rank r owns batches
+    [r*bl, (r+1)*bl) of A and B, multiplies them with the fp64 oracle into
+    its slice of C_full, and one all-gather (gloo, the same layout as the
+    in-place ncclAllGather) fills every rank's C_full.  Checked for both
+    config-4 shapes at reduced size."""
+    try:
+        import torch
+
+        from jstorch_b200 import synth
+        from oracle import oracle
+
+        d = _init_pg(rank, world, port)
+        ok = True
+        for (M, K, N) in ((32, 8, 32), (32, 32, 8)):
+            bl = 3
+            A = synth.matrix(3, synth.A, bl * world * M, K, "normal", 0.35).reshape(bl * world, M, K)
+            B = synth.matrix(3, synth.B, bl * world * K, N, "normal", 0.35).reshape(bl * world, K, N)
+            mine = slice(rank * bl, (rank + 1) * bl)
+            c_local = oracle.gemm_f64(A[mine], B[mine]).astype(np.float32)
+            parts = [torch.zeros((bl, M, N)) for _ in range(world)]
+            d.all_gather(parts, torch.from_numpy(c_local))
+            c_full = torch.cat(parts).numpy()
+            ref = oracle.gemm_f64(A, B).astype(np.float32)
+            ok = ok and np.array_equal(c_full, ref)
+        out_q.put((rank, "ok" if ok else "mismatch"))
+        d.destroy_process_group()
+    except Exception:
+        out_q.put((rank, traceback.format_exc()))
+
+
 def gloo_rank_dies(rank: int, world: int, port: int, out_q) -> None:
     """Failure path on the host: rank 1 leaves before the collective; rank 0's
     next collective must end with an error within the group timeout."""

@@ -60,6 +60,11 @@ def test_gloo_two_ranks_rowsharded_layout():
     assert out == {0: "ok", 1: "ok"}, out
 
 
+def test_gloo_two_ranks_batchsharded_layout():
+    out = _run(W.gloo_batchsharded_layout)
+    assert out == {0: "ok", 1: "ok"}, out
+
+
 def test_gloo_rank_leaves_survivor_errors():
     out = _run(W.gloo_rank_dies)
     assert out[1] == "left"
