@@ -184,3 +184,46 @@ def test_direct_1x1_leaves_col_buf_untouched():
     X, Wt = x.cpu().numpy(), w.cpu().numpy()
     one = (1, 1)
     _ok(out.cpu().numpy().astype(np.float64), oracle.conv2d_f64(X, Wt), _bound_conv2d(X, Wt, None, one, (0, 0), one, 1))
+
+
+GOLDEN_CONV = __import__("pathlib").Path(__file__).resolve().parent / "golden" / "ref_conv_int.npz"
+
+
+@pytest.mark.parametrize("kernel_path", ["auto"])
+def test_launchers_reproduce_reference_outputs_exactly(kernel_path):
+    """The fixtures of tests/golden/ref_conv_int.npz hold the reference's own
+    conv.cu launchers' outputs on integer-valued inputs (exact there).  Each of
+    this library's launchers, on the same inputs and geometry, must return the
+    same values bit for bit: small integers are exact in the 3xTF32 split and
+    in the FFMA kernel's fp32 accumulation."""
+    from jstorch_b200 import conv
+    gd = np.load(GOLDEN_CONV)
+    names = sorted({k.split("__")[0] for k in gd.files})
+    assert len(names) == 9
+    for name in names:
+        B, Ci, H, W, Co, kH, kW, sH, sW, pH, pW, dH, dW, g, opH, opW = [int(v) for v in gd[f"{name}__params"]]
+        one_d = H == 1 and kH == 1
+        x = gd[f"{name}__x"]
+        want = gd[f"{name}__out"]
+        if "bw" in name:
+            go = gd[f"{name}__go"]
+            if one_d:
+                fn = conv.conv_transpose1d_backward_weight if name.startswith("convT") else conv.conv1d_backward_weight
+                got = fn(_dev(x[:, :, 0]), _dev(go[:, :, 0]), kW, sW, pW, dW, g)
+            else:
+                fn = conv.conv_transpose2d_backward_weight if name.startswith("convT") else conv.conv2d_backward_weight
+                got = fn(_dev(x), _dev(go), (kH, kW), (sH, sW), (pH, pW), (dH, dW), g)
+        else:
+            w = gd[f"{name}__w"]
+            b = _dev(gd[f"{name}__bias"]) if f"{name}__bias" in gd.files else None
+            if one_d:
+                if name.startswith("convT"):
+                    got = conv.conv_transpose1d(_dev(x[:, :, 0]), _dev(w[:, :, 0]), b, sW, pW, opW, dW, g)
+                else:
+                    got = conv.conv1d(_dev(x[:, :, 0]), _dev(w[:, :, 0]), b, sW, pW, dW, g)
+            elif name.startswith("convT"):
+                got = conv.conv_transpose2d(_dev(x), _dev(w), b, (sH, sW), (pH, pW), (opH, opW), (dH, dW), g)
+            else:
+                got = conv.conv2d(_dev(x), _dev(w), b, (sH, sW), (pH, pW), (dH, dW), g)
+        got = _host(got).astype(np.float32).reshape(want.shape)
+        np.testing.assert_array_equal(got, want, err_msg=name)
