@@ -431,12 +431,15 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
     dist.barrier()
 
     timeline = None
-    if args.trace:  # one extra step with the library's event timeline (not timed)
+    if args.trace:  # one extra step with the library's event timeline on every rank (not timed)
         comm.trace(True)
+        dist.barrier()
         step()
         comm.sync(stream)
-        timeline = [(lab, round(ms, 3)) for lab, ms in comm.trace_read()]
+        mine = [(lab, round(ms, 3)) for lab, ms in comm.trace_read()]
         comm.trace(False)
+        timeline = [None] * world
+        dist.all_gather_object(timeline, mine)
 
     # end to end: this rank's A rows (and B on the root) in from pinned host
     # memory, the sharded GEMM, this rank's C rows back to pinned host memory
@@ -502,7 +505,7 @@ def run_jstorch_sharded(args, rank: int, world: int, local: int) -> None:
         "e2e": e2e, "roofline": roofline, "gpu_launches": int(tsum[1]), "clocks": clk,
     }
     if timeline:
-        line["timeline_rank0"] = timeline
+        line["timeline_ranks"] = timeline
     if reg:
         reg.deregister()
     del c
@@ -857,11 +860,38 @@ def run_config(args) -> None:
         torch.backends.cuda.matmul.allow_tf32 = False
         tf = lambda ms: flops / (ms * 1e-3) / 1e12
         per = lambda ks: {k: {"launches": v[0], "ms": v[1]} for k, v in ks.items()}
+
+        # two more layers of the same network: a 3x3 head with few output
+        # channels (its GEMM, M = 32, runs on the FFMA kernel over an explicit
+        # im2col column matrix) and a 2x2 stride-2 transposed convolution
+        # (col = W^T . x on tensor cores, then col2im with the bias)
+        w_head = torch.randn((32, Ci, 3, 3), device=dev, generator=gen) / 48.0
+        b_head = torch.randn(32, device=dev, generator=gen)
+        x_up = torch.randn((B, Ci, 28, 28), device=dev, generator=gen)
+        w_up = torch.randn((Ci, 128, 2, 2), device=dev, generator=gen) / 16.0
+        b_up = torch.randn(128, device=dev, generator=gen)
+        head = _time_device(lambda: conv.conv2d(x, w_head, b_head, 1, 1), args.steps, args.warmup, stream)
+        up = _time_device(lambda: conv.conv_transpose2d(x_up, w_up, b_up, 2, 0), args.steps, args.warmup, stream)
+        _lib.profile_enable(True)
+        _time_device(lambda: conv.conv2d(x, w_head, b_head, 1, 1), 3, 1, stream)
+        ks_h = _lib.profile_read()
+        _lib.profile_enable(True)
+        _time_device(lambda: conv.conv_transpose2d(x_up, w_up, b_up, 2, 0), 3, 1, stream)
+        ks_u = _lib.profile_read()
+        _lib.profile_enable(False)
+        head_flops = 2.0 * B * 32 * H * W * Ci * 9
+        up_flops = 2.0 * B * 128 * 4 * 28 * 28 * Ci
+        layers = {"head_3x3_256to32": {"ms": head, "tflops": head_flops / (head * 1e-3) / 1e12,
+                                       "kernels": per(ks_h), "path": "FFMA GEMM over an im2col column matrix"},
+                  "up_2x2s2_256to128_28to56": {"ms": up, "tflops": up_flops / (up * 1e-3) / 1e12,
+                                                "kernels": per(ks_u),
+                                                "path": "tensor-core col = W^T . x, then col2im + bias"}}
         out.update({"metric": "conv2d 3x3 256->256, 56x56, batch 32: forward (launch_conv2d)", "unit": "TFLOP/s",
                     "value": tf(fwd), "forward_ms": fwd, "backward_weight_ms": bwd,
                     "backward_weight_tflops": tf(bwd), "kernels_forward": per(ks_f),
                     "kernels_backward_weight": per(ks_b),
                     "kernels_note": "per-kernel totals over 3 calls, from an event-bracketed pass outside the timed one",
+                    "other_layers": layers,
                     "context": {"cudnn_fp32_ms": cudnn, "cudnn_fp32_tflops": tf(cudnn),
                                 "reference_design_tf32_ms": refd, "reference_design_tf32_tflops": tf(refd)},
                     "note": "context rows: torch cuDNN conv2d with TF32 off; the reference's im2col + per-image "
@@ -1071,9 +1101,10 @@ def run_jstorch(args) -> None:
     if not args.no_e2e:
         e2e = _e2e(args, A, B, stream)
 
-    # ---- roofline of the dominant kernel
+    # ---- roofline of the dominant kernel, against the peak of the clock
+    # regime its times were taken in (the event pass's own clock samples)
     peaks = _peaks()
-    peak, peak_kind = _tensor_peak(peaks, clk)
+    peak, peak_kind = _tensor_peak(peaks, pclk)
     burst = peaks["bf16_tflops"] / 6.0
     top = max(kstats.items(), key=lambda kv: kv[1][1]) if kstats else ("none", (0, 0.0))
     name, (nl, tot) = top

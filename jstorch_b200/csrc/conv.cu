@@ -109,6 +109,77 @@ __global__ void col2im_kernel(const float* __restrict__ col, float* __restrict__
     }
 }
 
+// The same sum with the taps tabulated once per block.  A tap (kh, kw) that
+// lands on output (h, w) reads col at (kh*kW + kw)*Ni + hi*Wo + wi, which
+// splits into a row part kh*kW*Ni + hi*Wo (valid kh, hi depend on h only) and
+// a column part kw*Ni + wi (kw, wi depend on w only).  The block builds, in
+// shared memory, the valid row parts of every output row and the valid column
+// parts of every output column (the only divides), then each output element
+// adds col[row part + column part] over its pairs in the order of
+// col2im_kernel (kh outer, kw inner), so the results are identical.
+// Shared memory: H*(1+kH) + W*(1+kW) ints; the host checks the size and that
+// the offsets fit an int.
+__global__ void col2im_tab_kernel(const float* __restrict__ col, float* __restrict__ out,
+                                  const float* __restrict__ bias, const Geo g) {
+    extern __shared__ int tab[];
+    int* rcnt = tab;                 // [H]
+    int* roff = rcnt + g.H;          // [H][kH]
+    int* ccnt = roff + g.H * g.kH;   // [W]
+    int* coff = ccnt + g.W;          // [W][kW]
+    const int Ni = g.Ho * g.Wo;
+    for (int h = threadIdx.x; h < g.H; h += blockDim.x) {
+        int n = 0;
+        for (int kh = 0; kh < g.kH; ++kh) {
+            const int nh = h + g.pH - kh * g.dH;
+            if (nh < 0 || nh % g.sH) continue;
+            const int hi = nh / g.sH;
+            if (hi >= g.Ho) continue;
+            roff[h * g.kH + n++] = kh * g.kW * Ni + hi * g.Wo;
+        }
+        rcnt[h] = n;
+    }
+    for (int w = threadIdx.x; w < g.W; w += blockDim.x) {
+        int n = 0;
+        for (int kw = 0; kw < g.kW; ++kw) {
+            const int nw = w + g.pW - kw * g.dW;
+            if (nw < 0 || nw % g.sW) continue;
+            const int wi = nw / g.sW;
+            if (wi >= g.Wo) continue;
+            coff[w * g.kW + n++] = kw * Ni + wi;
+        }
+        ccnt[w] = n;
+    }
+    __syncthreads();
+    const int64_t nplanes = (int64_t)g.B * g.C;
+    const int HW = g.H * g.W;
+    const int kk = g.kH * g.kW;
+    const int dh = blockDim.x / g.W, dw = blockDim.x % g.W;
+    for (int64_t bc = blockIdx.x + (int64_t)blockIdx.y * gridDim.x; bc < nplanes;
+         bc += (int64_t)gridDim.x * gridDim.y) {
+        const int c = (int)(bc % g.C);
+        const float* cb = col + bc * kk * Ni;
+        const float bv = bias ? __ldg(bias + c) : 0.0f;
+        float* o = out + bc * HW;
+        int h = threadIdx.x / g.W, w = threadIdx.x % g.W;
+        for (int i = threadIdx.x; i < HW; i += blockDim.x) {
+            float sum = 0.0f;
+            const int nr = rcnt[h], nc = ccnt[w];
+            for (int a = 0; a < nr; ++a) {
+                const float* rp = cb + roff[h * g.kH + a];
+                for (int q = 0; q < nc; ++q) sum += __ldg(rp + coff[w * g.kW + q]);
+            }
+            if (bias) sum += bv;
+            o[i] = sum;
+            h += dh;
+            w += dw;
+            if (w >= g.W) {
+                w -= g.W;
+                ++h;
+            }
+        }
+    }
+}
+
 // dst[c][b][n] = src[b][c][n], one block per (c, b) row
 __global__ void permute_bcn_kernel(const float* __restrict__ src, float* __restrict__ dst, int B, int C, int N) {
     const int64_t row = blockIdx.x + (int64_t)blockIdx.y * gridDim.x;  // c * B + b
@@ -302,7 +373,15 @@ int im2col(const float* in, float* col, const Geo& g, bool inner, cudaStream_t s
 int col2im(const float* col, float* out, const float* bias, const Geo& g, cudaStream_t s) {
     const int64_t planes = (int64_t)g.B * g.C;
     if (planes == 0 || (int64_t)g.H * g.W == 0) return JST_OK;
-    {
+    const size_t tab_bytes = ((size_t)g.H * (1 + g.kH) + (size_t)g.W * (1 + g.kW)) * sizeof(int);
+    const int64_t span = (int64_t)g.kH * g.kW * g.Ho * g.Wo;  // largest table offset
+    if (tab_bytes <= 32 * 1024 && span < 0x7fffffffLL) {
+        // one block per output plane up to 16 waves of 8 resident blocks,
+        // each block then walks planes (the tables are built once per block)
+        const int64_t blocks = std::min<int64_t>(planes, 148LL * 8 * 16);
+        ProfScope prof(s, KID_CONV);
+        col2im_tab_kernel<<<row_grid(blocks), 256, tab_bytes, s>>>(col, out, bias, g);
+    } else {
         ProfScope prof(s, KID_CONV);
         col2im_kernel<<<row_grid(planes), 256, 0, s>>>(col, out, bias, g);
     }

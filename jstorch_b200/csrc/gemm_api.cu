@@ -100,7 +100,14 @@ static bool use_tc(const GemmArgs& a) {
     // 2^28 multiply-adds (512^3, the nn.Linear layers of the MLP config); the
     // tensor-core kernel wins from 2^30 (64 x 512x512x64 batched, 2048^3 and up).
     const double macs = (double)a.M * a.N * a.K * a.batch;
-    return a.M >= 64 && a.N >= 64 && a.K >= 32 && macs >= 1073741824.0;
+    if (a.K < 32) return false;
+    if (a.M >= 64 && a.N >= 64) return macs >= 1073741824.0;
+    // A narrow side of 16..63 pads the tensor-core tile (128 rows, 64 columns
+    // at least) to a quarter or half full, but the FFMA kernel's tiles are
+    // padded as well and its peak is a quarter of the 3xTF32 rate, so large
+    // products still belong on the tensor cores (a 3x3 convolution with 32
+    // output channels, M = 32 over 32 x 3136 x 2304: FFMA 7.9 TFLOP/s).
+    return a.M >= 16 && a.N >= 16 && macs >= 4294967296.0;
 }
 
 static int validate(const jst_gemm_desc* d, GemmArgs* a) {

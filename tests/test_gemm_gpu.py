@@ -197,6 +197,11 @@ def test_kernel_choice_heuristic(jst):
     assert jst.select_kernel(256, 1024, 784) == "ffma"
     assert jst.select_kernel(256, 10, 1024) == "ffma"
     assert jst.select_kernel(2, 4, 3) == "ffma"
+    # a narrow side of 16..63 goes to the tensor cores once the product is large
+    assert jst.select_kernel(32, 3136, 2304, batch=32) == "tc3xtf32"
+    assert jst.select_kernel(4096, 48, 8192, batch=8) == "tc3xtf32"
+    assert jst.select_kernel(32, 3136, 2304) == "ffma"
+    assert jst.select_kernel(8, 3136, 2304, batch=64) == "ffma"
 
 
 @pytest.mark.parametrize("pinned", [False, True])
@@ -446,3 +451,17 @@ def test_operands_written_by_the_previous_kernel(jst, kernel, M, N, K):
         jst.gemm(a, b, out=c, kernel=kernel)
         checks.append((c == v * 0.5 * K).all())  # exact: every product and sum is representable
     assert all(bool(x) for x in checks)
+
+
+@pytest.mark.parametrize("M,N,K,batch", [(20, 5000, 1000, 48), (3000, 40, 2000, 24)])
+def test_narrow_side_on_tensor_cores_matches_oracle(jst, M, N, K, batch):
+    """A narrow M or N (16..63) with a large product runs on the tensor-core
+    kernel with a partly filled tile; every element is checked."""
+    import torch
+    assert jst.select_kernel(M, N, K, batch=batch) == "tc3xtf32"
+    rng = np.random.default_rng(M + N)
+    A = rng.standard_normal((batch, M, K), dtype=np.float32)
+    B = rng.standard_normal((batch, K, N), dtype=np.float32)
+    c = jst.gemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
+    err, where = oracle.max_rel_err(A, B, c.cpu().numpy(), oracle.gemm_f64(A, B))
+    assert err <= TOL, (err, where)
