@@ -104,6 +104,7 @@ struct Params {
     int kslices;           // > 1: split K; C receives partials [slice][batch][M][N]
     int kb_per_slice;      // BK steps per slice
     int split_a;           // tm_a_hi maps the raw fp32 A; the epilogue warps split it in shared memory
+    int tma_store;         // persistent kernel: C is written by TMA stores through tm_c
 };
 
 __device__ __forceinline__ float epi(float v, const float* bias, int col, int relu) {
@@ -359,6 +360,370 @@ __global__ void __launch_bounds__(THREADS, C::MIN_BLOCKS)
     if (threadIdx.x == 0 && *err != 0) atomicOr(p.err, *err);
 }
 
+// --------------------------------------------------------------- persistent narrow tiles
+// For narrow outputs (BN = 64 / 128) with many tiles, one CTA per SM walks
+// its share of the output tiles instead of one CTA per tile.  A one-tile CTA
+// spends its life in two serial phases -- the TMA round trips of its few
+// k-slabs, then an epilogue that stores the whole tile -- and since all CTAs
+// of a wave start together, every SM loads at the same time and then stores
+// at the same time (measured on 64 x [512x64].[64x512]: 2.0 + 2.2 us of load
+// round trips and 3.9 us of stores per 9.3 us CTA).  Here the phases of
+// consecutive tiles overlap inside the CTA:
+//   warp 0      TMA producer: runs ahead through the k-slabs of all its
+//               tiles, as far as the STAGES-deep ring allows;
+//   warp 1      TMEM allocation + MMA issuer: two accumulator buffers (each a
+//               D_hi and a D_lo of BN columns), so tile i + 1 accumulates
+//               while the epilogue drains tile i;
+//   warps 2-9   epilogue, two warps per TMEM lane quadrant taking alternate
+//               32-column chunks: drain a buffer, release it, fused epilogue,
+//               then each 32 x 32 block goes out as one TMA store from a
+//               128-byte swizzled staging block (own staging area);
+//   warps 10-13 split of the raw K-major A tile into hi / lo in place (split_a).
+// Same arithmetic, epilogues and results as tc_gemm_kernel with one K slice.
+template <int BN_, int STAGES_>
+struct PCfg {
+    static constexpr int BN = BN_;
+    static constexpr int STAGES = STAGES_;
+    static constexpr uint32_t ACC_COLS = 2 * BN_;        // D_hi | D_lo of one buffer
+    static constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;  // two buffers: 256 or 512 columns
+    static constexpr uint32_t A_TILE_BYTES = BM * BK * 4;
+    static constexpr uint32_t B_TILE_BYTES = BN_ * BK * 4;
+    static constexpr uint32_t STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;
+    static constexpr uint32_t RING_BYTES = STAGES_ * STAGE_BYTES;
+    // epilogue staging: per epilogue warp two 32 x 32 fp32 blocks (4 KiB each,
+    // 128-byte swizzled rows) for the TMA stores, or the STG_LD-pitched block
+    // of the element-store path
+    static constexpr uint32_t STG_OFF = RING_BYTES;  // a multiple of 1024
+    static constexpr uint32_t STG_P_BYTES = 8 * 2 * 4096;
+    static_assert(STG_P_BYTES >= STG_BYTES, "staging");
+    static constexpr uint32_t BAR_OFF = STG_OFF + STG_P_BYTES;
+    static constexpr uint32_t SMEM_BYTES = BAR_OFF + 512 + 1024 /*align slack*/;
+    static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation is a power of two");
+    static_assert(3 * STAGES_ + 5 <= 56, "barrier area");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+};
+constexpr int PTHREADS = 448;  // 14 warps; at most 146 registers a thread
+using PCfgMid = PCfg<128, 4>;
+using PCfgNarrow = PCfg<64, 6>;
+
+// Output tile t of a one-slice GEMM: batch index and first row / column
+// (grouped rasterisation in bands of 16 tile rows, as tc_gemm_kernel).
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int bn, int* bidx, int* m0, int* n0) {
+    const int per_batch = p.tiles_m * p.tiles_n;
+    const int tt = t % per_batch;
+    *bidx = t / per_batch;
+    constexpr int GROUP = 16;
+    const int span = GROUP * p.tiles_n;
+    const int g = tt / span;
+    const int first_m = g * GROUP;
+    const int gm = min(p.tiles_m - first_m, GROUP);
+    *m0 = (first_m + (tt % span) % gm) * BM;
+    *n0 = ((tt % span) / gm) * bn;
+}
+
+template <class C>
+__global__ void __launch_bounds__(PTHREADS, 1)
+    tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap tm_a_hi, const __grid_constant__ CUtensorMap tm_a_lo,
+                           const __grid_constant__ CUtensorMap tm_b_hi, const __grid_constant__ CUtensorMap tm_b_lo,
+                           const __grid_constant__ CUtensorMap tm_c, const Params p) {
+    constexpr int BN = C::BN;
+    constexpr int STAGES = C::STAGES;
+    constexpr uint32_t ACC_COLS = C::ACC_COLS, TMEM_COLS = C::TMEM_COLS;
+    constexpr uint32_t A_TILE_BYTES = C::A_TILE_BYTES, B_TILE_BYTES = C::B_TILE_BYTES;
+    constexpr uint32_t STAGE_BYTES = C::STAGE_BYTES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+    uint64_t* empty_bar = full_bar + STAGES;
+    uint64_t* conv_bar = empty_bar + STAGES;  // split_a: the stage's A tile has been split
+    uint64_t* accf_bar = conv_bar + STAGES;   // [2] accumulator buffer complete (MMA -> epilogue)
+    uint64_t* acce_bar = accf_bar + 2;        // [2] accumulator buffer drained (epilogue -> MMA)
+    uint64_t* done_bar = acce_bar + 2;        // every MMA of this CTA has completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+    volatile uint32_t* err = tmem_slot + 1;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int total = p.tiles_m * p.tiles_n * p.batch;
+    const int num_kb = (p.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            ptx::mbar_init(&full_bar[s], 1);
+            ptx::mbar_init(&empty_bar[s], 1);
+            ptx::mbar_init(&conv_bar[s], 4);  // one arrival per splitting warp
+        }
+        for (int b = 0; b < 2; ++b) {
+            ptx::mbar_init(&accf_bar[b], 1);
+            ptx::mbar_init(&acce_bar[b], 8);  // one arrival per epilogue warp
+        }
+        ptx::mbar_init(done_bar, 1);
+        *err = 0;
+        ptx::fence_barrier_init();
+        ptx::tma_prefetch_desc(&tm_a_hi);
+        ptx::tma_prefetch_desc(&tm_a_lo);
+        ptx::tma_prefetch_desc(&tm_b_hi);
+        ptx::tma_prefetch_desc(&tm_b_lo);
+        if (p.tma_store) ptx::tma_prefetch_desc(&tm_c);
+    }
+    if (warp == 1) ptx::tmem_alloc<TMEM_COLS>(tmem_slot);
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    ptx::griddep_wait();
+    ptx::griddep_launch_dependents();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer
+            uint32_t g = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                int bidx, m0, n0;
+                tile_coords(t, p, BN, &bidx, &m0, &n0);
+                const int za = p.a_bcast ? 0 : bidx, zb = p.b_bcast ? 0 : bidx;
+                for (int kb = 0; kb < num_kb; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    const uint32_t phase = (g / STAGES) & 1;
+                    if (!ptx::mbar_wait(&empty_bar[s], phase ^ 1, err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + s * STAGE_BYTES;
+                    ptx::mbar_arrive_expect_tx(&full_bar[s], p.split_a ? STAGE_BYTES - A_TILE_BYTES : STAGE_BYTES);
+                    const int kx = kb * BK;
+                    ptx::tma_load_3d(st, &tm_a_hi, &full_bar[s], kx, m0, za);
+                    if (!p.split_a) ptx::tma_load_3d(st + A_TILE_BYTES, &tm_a_lo, &full_bar[s], kx, m0, za);
+                    ptx::tma_load_3d(st + 2 * A_TILE_BYTES, &tm_b_hi, &full_bar[s], kx, n0, zb);
+                    ptx::tma_load_3d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_b_lo, &full_bar[s], kx, n0, zb);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN);
+            uint32_t g = 0;
+            bool ok = true;
+            int i = 0;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
+                const int buf = i & 1;
+                // the epilogue has drained this buffer's previous tile
+                if (!ptx::mbar_wait(&acce_bar[buf], ((i >> 1) & 1) ^ 1, err)) break;
+                ptx::tc_fence_after();
+                const uint32_t d_hi = tmem_base + buf * ACC_COLS, d_lo = d_hi + BN;
+                for (int kb = 0; kb < num_kb; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    const uint32_t phase = (g / STAGES) & 1;
+                    if (!ptx::mbar_wait(p.split_a ? &conv_bar[s] : &full_bar[s], phase, err)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    const uint32_t st = ptx::smem_u32(smem + s * STAGE_BYTES);
+                    const uint32_t a_hi = st, a_lo = st + A_TILE_BYTES;
+                    const uint32_t b_hi = st + 2 * A_TILE_BYTES, b_lo = b_hi + B_TILE_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        const uint32_t off = kk * 32;
+                        const uint32_t acc0 = (kb | kk) != 0;
+                        const uint64_t dah = ptx::smem_desc_kmajor(a_hi + off, 64);
+                        const uint64_t dbh = ptx::smem_desc_kmajor(b_hi + off, 64);
+                        ptx::mma_tf32(d_lo, ptx::smem_desc_kmajor(a_lo + off, 64), dbh, idesc, acc0);
+                        ptx::mma_tf32(d_lo, dah, ptx::smem_desc_kmajor(b_lo + off, 64), idesc, 1);
+                        ptx::mma_tf32(d_hi, dah, dbh, idesc, acc0);
+                    }
+                    ptx::mma_commit(&empty_bar[s]);  // slot s is free once these MMAs finish
+                }
+                if (ok) ptx::mma_commit(&accf_bar[buf]);
+            }
+            // every MMA issued here completes before the TMEM is released
+            ptx::mma_commit(done_bar);
+            ptx::mbar_wait(done_bar, 0, err);
+        }
+    } else if (warp >= 10) {
+        // ---------------------------------------------------- A split (split_a)
+        if (p.split_a) {
+            const int ct = threadIdx.x - 320;  // 0..127
+            uint32_t g = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+                for (int kb = 0; kb < num_kb; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    const uint32_t phase = (g / STAGES) & 1;
+                    int okw = 0;
+                    if (lane == 0) okw = ptx::mbar_wait(&full_bar[s], phase, err);
+                    if (!__shfl_sync(0xffffffffu, okw, 0)) {
+                        ok = false;
+                        break;
+                    }
+                    float4* hi = reinterpret_cast<float4*>(smem + s * STAGE_BYTES);
+                    float4* lo = reinterpret_cast<float4*>(smem + s * STAGE_BYTES + A_TILE_BYTES);
+#pragma unroll
+                    for (int k = 0; k < (int)(A_TILE_BYTES / 16) / 128; ++k) {
+                        const int idx = ct + k * 128;
+                        const float4 v = hi[idx];
+                        float4 h, l;
+                        h.x = ptx::to_tf32(v.x); l.x = ptx::to_tf32(v.x - h.x);
+                        h.y = ptx::to_tf32(v.y); l.y = ptx::to_tf32(v.y - h.y);
+                        h.z = ptx::to_tf32(v.z); l.z = ptx::to_tf32(v.z - h.z);
+                        h.w = ptx::to_tf32(v.w); l.w = ptx::to_tf32(v.w - h.w);
+                        hi[idx] = h;
+                        lo[idx] = l;
+                    }
+                    ptx::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(&conv_bar[s]);
+                }
+            }
+        }
+    } else {
+        // ---------------------------------------------------- epilogue (warps 2-9)
+        const int q = warp & 3;           // TMEM lane quadrant this warp may access
+        const int half = (warp - 2) >> 2;  // 0: even 32-column chunks, 1: odd
+        float* stg = reinterpret_cast<float*>(smem + C::STG_OFF) + (warp - 2) * (32 * STG_LD);
+        uint8_t* tstg = smem + C::STG_OFF + (warp - 2) * 2 * 4096;  // two swizzled 4 KiB blocks
+        uint32_t nstore = 0;  // TMA stores issued by this warp
+        const bool row_bias = p.bias_row && p.bias;
+        const float* cbias = p.bias_row ? nullptr : p.bias;
+        const bool vec = ((p.ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                         ((p.strideC & 3) == 0);
+        int i = 0;
+        for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+            const int buf = i & 1;
+            int okw = 0;
+            if (lane == 0) okw = ptx::mbar_wait(&accf_bar[buf], (i >> 1) & 1, err) && *err == 0;
+            if (!__shfl_sync(0xffffffffu, okw, 0)) break;
+            ptx::tc_fence_after();
+            int bidx, m0, n0;
+            tile_coords(t, p, BN, &bidx, &m0, &n0);
+            const int row = m0 + q * 32 + lane;
+            const bool row_ok = row < p.M;
+            float* cbase = p.C + (int64_t)bidx * p.strideC;
+            float* crow = cbase + (int64_t)row * p.ldc;
+            const float rbias = (row_bias && row_ok) ? __ldg(p.bias + row) : 0.0f;
+            const float* abase = p.aux ? p.aux + (int64_t)bidx * p.stride_aux : nullptr;
+            const int nchunks = min(BN / 32, (p.N - n0 + 31) / 32);
+            // this warp's chunks: c = half, half + 2, ...; a warp with none
+            // still releases the buffer
+            const int last = nchunks - 1 - ((nchunks - 1 - half) & 1);
+            if (last < 0) {
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(&acce_bar[buf]);
+            }
+#pragma unroll 1
+            for (int c = half; c < nchunks; c += 2) {
+                const int col0 = n0 + c * 32;
+                uint32_t r[32], rl[32];
+                const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + buf * ACC_COLS + (uint32_t)(c * 32);
+                ptx::tmem_ld_32x32b_x32(taddr, r);
+                ptx::tmem_ld_32x32b_x32(taddr + BN, rl);
+                ptx::tmem_ld_wait();
+                if (c == last) {  // this warp is done with the buffer: the MMA may reuse it once all are
+                    ptx::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) ptx::mbar_arrive(&acce_bar[buf]);
+                }
+                // a non-finite D_hi is the result (see tc_gemm_kernel)
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const uint32_t h = r[j];
+                    if ((h & 0x7f800000u) != 0x7f800000u) r[j] = __float_as_uint(__uint_as_float(h) + __uint_as_float(rl[j]));
+                }
+                if (row_bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + rbias);
+                }
+                if (p.tma_store) {  // warp-uniform; no mask epilogue on this path
+                    // row `lane` of the block into a 128-byte swizzled staging
+                    // row (16-byte chunk j at j ^ (lane & 7): conflict-free),
+                    // then one TMA store of the 32 x 32 block; the box parts
+                    // past M or N are not written, and a block wholly past M
+                    // is not stored
+                    if (m0 + q * 32 < p.M) {
+                        uint8_t* blk = tstg + (nstore & 1) * 4096;
+                        if (lane == 0) ptx::bulk_wait_read<1>();  // the store that used `blk` has read it
+                        __syncwarp();
+                        const float* cb = (cbias && col0 + 32 <= p.N) ? cbias : nullptr;  // partial chunk below
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            float4 v;
+                            v.x = epi(__uint_as_float(r[4 * j + 0]), cb, col0 + 4 * j + 0, p.relu);
+                            v.y = epi(__uint_as_float(r[4 * j + 1]), cb, col0 + 4 * j + 1, p.relu);
+                            v.z = epi(__uint_as_float(r[4 * j + 2]), cb, col0 + 4 * j + 2, p.relu);
+                            v.w = epi(__uint_as_float(r[4 * j + 3]), cb, col0 + 4 * j + 3, p.relu);
+                            if (cbias && !cb) {  // last chunk of a ragged N: bias only where it exists
+                                const int c4 = col0 + 4 * j;
+                                v.x = c4 + 0 < p.N ? epi(__uint_as_float(r[4 * j + 0]), cbias, c4 + 0, p.relu) : 0.0f;
+                                v.y = c4 + 1 < p.N ? epi(__uint_as_float(r[4 * j + 1]), cbias, c4 + 1, p.relu) : 0.0f;
+                                v.z = c4 + 2 < p.N ? epi(__uint_as_float(r[4 * j + 2]), cbias, c4 + 2, p.relu) : 0.0f;
+                                v.w = c4 + 3 < p.N ? epi(__uint_as_float(r[4 * j + 3]), cbias, c4 + 3, p.relu) : 0.0f;
+                            }
+                            *reinterpret_cast<float4*>(blk + lane * 128 + ((j ^ (lane & 7)) << 4)) = v;
+                        }
+                        ptx::fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            ptx::tma_store_3d(&tm_c, blk, col0, m0 + q * 32, bidx);
+                            ptx::bulk_commit();
+                        }
+                        ++nstore;
+                    }
+                } else if (vec && col0 + 32 <= p.N) {  // warp-uniform
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        float4 v;
+                        v.x = epi(__uint_as_float(r[j + 0]), cbias, col0 + j + 0, p.relu);
+                        v.y = epi(__uint_as_float(r[j + 1]), cbias, col0 + j + 1, p.relu);
+                        v.z = epi(__uint_as_float(r[j + 2]), cbias, col0 + j + 2, p.relu);
+                        v.w = epi(__uint_as_float(r[j + 3]), cbias, col0 + j + 3, p.relu);
+                        *reinterpret_cast<float4*>(stg + lane * STG_LD + j) = v;
+                    }
+                    __syncwarp();
+#pragma unroll
+                    for (int it = 0; it < 8; ++it) {
+                        const int rr = it * 4 + (lane >> 3);
+                        const int cc = (lane & 7) * 4;
+                        float4 v = *reinterpret_cast<const float4*>(stg + rr * STG_LD + cc);
+                        const int grow = m0 + q * 32 + rr;
+                        if (grow < p.M) {
+                            if (abase) {
+                                const float* ar = abase + (int64_t)grow * p.ld_aux + col0 + cc;
+                                if (!(__ldg(ar + 0) > 0.0f)) v.x = 0.0f;
+                                if (!(__ldg(ar + 1) > 0.0f)) v.y = 0.0f;
+                                if (!(__ldg(ar + 2) > 0.0f)) v.z = 0.0f;
+                                if (!(__ldg(ar + 3) > 0.0f)) v.w = 0.0f;
+                            }
+                            *reinterpret_cast<float4*>(cbase + (int64_t)grow * p.ldc + col0 + cc) = v;
+                        }
+                    }
+                    __syncwarp();  // the staging tile is rewritten by the next chunk
+                } else if (row_ok) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (col0 + j >= p.N) continue;
+                        float v = epi(__uint_as_float(r[j]), cbias, col0 + j, p.relu);
+                        if (abase && !(__ldg(abase + (int64_t)row * p.ld_aux + col0 + j) > 0.0f)) v = 0.0f;
+                        crow[col0 + j] = v;
+                    }
+                }
+            }
+        }
+        if (lane == 0 && nstore) ptx::bulk_wait_all();  // C is written before the CTA exits
+    }
+
+    ptx::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc<TMEM_COLS>(tmem_base);
+    }
+    if (threadIdx.x == 0 && *err != 0) atomicOr(p.err, *err);
+}
+
 // --------------------------------------------------------------- split passes
 // Source K-major: element (b, r, k) at src[b*sstride + r*ld + k].
 template <bool VEC>
@@ -486,6 +851,23 @@ static bool make_raw_map(CUtensorMap* m, const float* base, int K, int rows, int
     return r == CUDA_SUCCESS;
 }
 
+// 3-D map over C [batch][M][ldc] for TMA stores of 32 x 32 blocks (128-byte
+// swizzled rows in shared memory).  False when C's base or strides are not
+// 16-byte multiples.
+static bool make_c_map(CUtensorMap* m, float* C, int M, int N, int batch, int64_t ldc, int64_t strideC) {
+    if ((reinterpret_cast<uintptr_t>(C) & 15) || (ldc & 3) || (batch > 1 && (strideC & 3))) return false;
+    auto enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)batch};
+    const int64_t bs = batch > 1 ? strideC : ldc * M;
+    cuuint64_t strides[2] = {(cuuint64_t)ldc * 4, (cuuint64_t)bs * 4};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, C, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 static int launch_split(const float* src, bool kmajor, int64_t ld, int64_t sstride, int rows, int K, int Kp,
                         int batch, float* hi, float* lo, cudaStream_t s) {
     if (rows == 0 || Kp == 0) return JST_OK;
@@ -599,6 +981,67 @@ static int launch_cfg(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CU
     return JST_OK;
 }
 
+// Launch the persistent narrow-tile kernel on `grid` CTAs (one per SM).
+template <class Cf>
+static int launch_persist(const CUtensorMap& a_hi, const CUtensorMap& a_lo, const CUtensorMap& b_hi,
+                          const CUtensorMap& b_lo, const CUtensorMap& c_map, const tc::Params& p, unsigned grid,
+                          cudaStream_t s, bool pdl) {
+    static bool attr_set[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+            if (cudaFuncSetAttribute(tc::tc_gemm_persist_kernel<Cf>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Cf::SMEM_BYTES) != cudaSuccess)
+                return set_status(JST_ERR_CUDA, "cudaFuncSetAttribute(tc_gemm_persist_kernel) failed");
+            attr_set[dev] = true;
+        }
+    }
+    {
+        ProfScope prof(s, KID_TC_GEMM);
+        if (pdl) {
+            if (launch_dependent(tc::tc_gemm_persist_kernel<Cf>, dim3(grid), dim3(tc::PTHREADS), Cf::SMEM_BYTES, s,
+                                 a_hi, a_lo, b_hi, b_lo, c_map, p) != cudaSuccess)
+                return set_status(JST_ERR_CUDA, "tc_gemm_persist_kernel launch failed");
+        } else {
+            tc::tc_gemm_persist_kernel<Cf><<<grid, tc::PTHREADS, Cf::SMEM_BYTES, s>>>(a_hi, a_lo, b_hi, b_lo, c_map,
+                                                                                      p);
+        }
+    }
+    if (cudaPeekAtLastError() != cudaSuccess) return set_status(JST_ERR_CUDA, "tc_gemm_persist_kernel launch failed");
+    return JST_OK;
+}
+
+// SMs of the current device (the persistent kernel's grid).
+static int sm_count() {
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return 148;
+    }
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = 148;
+        }
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+// Narrow tiles (64 / 128 columns) in one K slice, written straight to C, and
+// at least two tiles per SM: the persistent kernel overlaps each tile's
+// epilogue with the next tile's loads and MMAs.  With fewer tiles a CTA per
+// tile spreads the work over more SMs (64 x [512x512].[512x64]: 256 tiles of
+// 32 k-slabs ran 31 us one per CTA, 43 us two per persistent CTA).
+static bool use_persistent(int bn, int64_t tiles, int kslices, int mc_store) {
+    return kslices == 1 && !mc_store && bn <= 128 && tiles >= 2LL * sm_count();
+}
+
 int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo, int M, int N, int K,
                    int batch, float* C, int64_t ldc, int64_t strideC, const float* bias, int relu, uint32_t* err,
                    cudaStream_t s, int mc_store, const float* aux, int64_t ld_aux, int64_t stride_aux, int bias_row,
@@ -637,9 +1080,20 @@ int tc_gemm_planes(const float* a_hi, const float* a_lo, const float* b_hi, cons
     p.kslices = kslices;
     p.kb_per_slice = kb_per_slice;
     p.split_a = split_a;
+    p.tma_store = 0;
     const int64_t grid = (int64_t)p.tiles_m * p.tiles_n * batch * kslices;
     if (grid > 0x7fffffff) return set_status(JST_ERR_ARG, "tc: too many tiles");
     int rc;
+    if (use_persistent(bn, grid, kslices, mc_store)) {
+        // C through TMA stores when its layout allows them (16-byte aligned
+        // base and strides) and no mask is read; element stores otherwise
+        CUtensorMap m_c = m_ahi;  // not read unless tma_store
+        p.tma_store = !aux && make_c_map(&m_c, C, M, N, batch, ldc, strideC) ? 1 : 0;
+        const unsigned pgrid = (unsigned)std::min<int64_t>(grid, sm_count());
+        if (bn == 128) rc = launch_persist<PCfgMid>(m_ahi, m_alo, m_bhi, m_blo, m_c, p, pgrid, s, pdl != 0);
+        else rc = launch_persist<PCfgNarrow>(m_ahi, m_alo, m_bhi, m_blo, m_c, p, pgrid, s, pdl != 0);
+        return rc;
+    }
     if (bn == 256) rc = launch_cfg<CfgWide>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s, pdl != 0);
     else if (bn == 128) rc = launch_cfg<CfgMid>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s, pdl != 0);
     else rc = launch_cfg<CfgNarrow>(m_ahi, m_alo, m_bhi, m_blo, p, (unsigned)grid, s, pdl != 0);

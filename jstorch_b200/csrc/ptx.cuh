@@ -101,6 +101,24 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
         : "memory");
 }
 
+// 3-D tiled bulk tensor store this CTA's shared memory -> global, tracked in
+// the issuing thread's bulk groups.  x (innermost) times 4 bytes is a multiple
+// of 16 and every coordinate is >= 0 at every call site; the box parts outside
+// the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(tmap),
+                 "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until all of this thread's bulk groups have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ------------------------------------------- programmatic dependent launch
 // Wait until the grids this one depends on (launched before it with the
 // programmatic-serialization attribute) have completed and their writes are

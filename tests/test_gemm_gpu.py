@@ -465,3 +465,125 @@ def test_narrow_side_on_tensor_cores_matches_oracle(jst, M, N, K, batch):
     c = jst.gemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
     err, where = oracle.max_rel_err(A, B, c.cpu().numpy(), oracle.gemm_f64(A, B))
     assert err <= TOL, (err, where)
+
+
+def _gemm_desc(a, b, c, M, N, K, batch, *, ta=False, tb=False, sa=None, sb=None, ldc=None, sc=None):
+    from jstorch_b200 import _lib
+    d = _lib.GemmDesc()
+    _lib.load().jst_gemm_desc_init(ctypes.byref(d), M, N, K, a.data_ptr(), b.data_ptr(), c.data_ptr())
+    d.transA, d.transB = int(ta), int(tb)
+    d.lda = M if ta else K
+    d.ldb = K if tb else N
+    d.ldc = ldc if ldc is not None else N
+    d.batch = batch
+    d.strideA = M * K if sa is None else sa
+    d.strideB = K * N if sb is None else sb
+    d.strideC = M * d.ldc if sc is None else sc
+    d.kernel = _lib.KERNEL_TC3XTF32
+    return d
+
+
+@pytest.mark.parametrize("M,N,K,batch,ta,tb,bcast_a", [
+    (512, 512, 64, 64, False, False, False),    # config 4 scores: 1024 tiles of 128 x 128, K = 4 slabs
+    (512, 64, 512, 80, False, False, False),    # config 4's output shape, 320 tiles of 128 x 64
+    (300, 100, 97, 100, False, False, False),   # ragged M / N / K, 128-wide tiles
+    (1000, 60, 333, 40, False, False, False),   # ragged, 64-wide tiles
+    (256, 128, 200, 150, True, False, False),   # A stored [K, M]: A planes from the split pass
+    (384, 96, 130, 100, False, True, False),    # B stored [N, K]
+    (128, 128, 288, 300, False, False, True),   # broadcast A (a convolution's weights)
+])
+def test_persistent_narrow_tiles_match_one_tile_kernel(jst, M, N, K, batch, ta, tb, bcast_a):
+    """At least one narrow output tile per SM runs the persistent kernel (one
+    CTA per SM walking tiles, double-buffered accumulators).  One batch entry
+    alone has too few tiles for it and runs the one-tile-per-CTA kernel: both
+    do the same arithmetic, so C must match bit for bit; and the batched
+    result meets the oracle bound."""
+    import torch
+    from jstorch_b200 import _lib
+    lib = _lib.load()
+    rng = np.random.default_rng(M * 3 + N + K)
+    A = _rand(rng, 1 if bcast_a else batch, *((K, M) if ta else (M, K)))
+    B = _rand(rng, batch, *((N, K) if tb else (K, N)))
+    a, b = _dev(A), _dev(B)
+    c = torch.full((batch, M, N), float("nan"), device="cuda")
+    d = _gemm_desc(a, b, c, M, N, K, batch, ta=ta, tb=tb, sa=0 if bcast_a else None)
+    _lib.check(lib.jst_gemm_ex(ctypes.byref(d)))
+    for i in (0, batch // 2, batch - 1):  # one entry at a time: the one-tile kernel
+        ci = torch.full((1, M, N), float("nan"), device="cuda")
+        ai = a[0 if bcast_a else i:(0 if bcast_a else i) + 1]
+        di = _gemm_desc(ai, b[i:i + 1], ci, M, N, K, 1, ta=ta, tb=tb)
+        _lib.check(lib.jst_gemm_ex(ctypes.byref(di)))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(c[i].cpu().numpy(), ci[0].cpu().numpy())
+    C = c.cpu().numpy()
+    assert np.isfinite(C).all()
+    for i in range(0, batch, max(1, batch // 6)):
+        _check(A[0 if bcast_a else i], B[i], C[i], ta=ta, tb=tb, rows=np.arange(0, M, 7))
+
+
+@pytest.mark.parametrize("epi", ["bias_relu", "row_bias", "mask"])
+def test_persistent_narrow_tiles_epilogues(jst, epi):
+    import torch
+    from jstorch_b200 import _lib
+    lib = _lib.load()
+    M, N, K, batch = 260, 120, 72, 100
+    rng = np.random.default_rng(7)
+    A, B = _rand(rng, batch, M, K), _rand(rng, batch, K, N)
+    a, b = _dev(A), _dev(B)
+    c = torch.full((batch, M, N), float("nan"), device="cuda")
+    d = _gemm_desc(a, b, c, M, N, K, batch)
+    if epi == "bias_relu":
+        bias = _rand(rng, N)
+        db = _dev(bias)
+        d.bias, d.epilogue = db.data_ptr(), _lib.EPI_BIAS | _lib.EPI_RELU
+    elif epi == "row_bias":
+        bias = _rand(rng, M)
+        db = _dev(bias)
+        d.bias, d.epilogue = db.data_ptr(), 8  # JST_EPI_BIAS_ROW
+    else:
+        aux = _rand(rng, batch, M, N)
+        daux = _dev(aux)
+        d.aux, d.ld_aux, d.stride_aux, d.epilogue = daux.data_ptr(), N, M * N, 4  # JST_EPI_MASK
+    _lib.check(lib.jst_gemm_ex(ctypes.byref(d)))
+    torch.cuda.synchronize()
+    C = c.cpu().numpy().astype(np.float64)
+    for i in (0, 17, batch - 1):
+        ref = oracle.gemm_f64(A[i], B[i])
+        if epi == "bias_relu":
+            ref = np.maximum(ref + bias[None, :], 0.0)
+            err, w = oracle.max_rel_err(A[i], B[i], C[i], ref, bias=bias)
+        elif epi == "row_bias":
+            ref = ref + bias[:, None]
+            mag = np.sqrt(np.square(A[i].astype(np.float64)).sum(1))[:, None] * \
+                np.sqrt(np.square(B[i].astype(np.float64)).sum(0))[None, :] + np.abs(bias)[:, None]
+            err = float(np.max(np.abs(C[i] - ref) / mag))
+        else:
+            ref = ref * (aux[i] > 0)
+            err, w = oracle.max_rel_err(A[i], B[i], C[i], ref)
+        assert err <= TOL, (epi, i, err)
+
+
+def test_persistent_narrow_tiles_unaligned_ldc(jst):
+    """C rows not 16-byte aligned (ldc odd) take the element-store path, an
+    aligned C the TMA-store path: same values bit for bit, padding columns
+    untouched, and the oracle bound."""
+    import torch
+    from jstorch_b200 import _lib
+    lib = _lib.load()
+    M, N, K, batch, ldc = 256, 100, 64, 150, 101
+    rng = np.random.default_rng(9)
+    A, B = _rand(rng, batch, M, K), _rand(rng, batch, K, N)
+    a, b = _dev(A), _dev(B)
+    cbuf = torch.full((batch * M * ldc,), float("nan"), device="cuda")
+    d = _gemm_desc(a, b, cbuf, M, N, K, batch, ldc=ldc)
+    _lib.check(lib.jst_gemm_ex(ctypes.byref(d)))
+    c_al = torch.full((batch, M, 104), float("nan"), device="cuda")  # ldc 104: 16-byte rows
+    d2 = _gemm_desc(a, b, c_al, M, N, K, batch, ldc=104)
+    _lib.check(lib.jst_gemm_ex(ctypes.byref(d2)))
+    torch.cuda.synchronize()
+    C = cbuf.cpu().numpy().reshape(batch, M, ldc)
+    C2 = c_al.cpu().numpy()
+    assert np.isnan(C[:, :, N:]).all() and np.isnan(C2[:, :, N:]).all()  # the padding columns are untouched
+    np.testing.assert_array_equal(C[:, :, :N], C2[:, :, :N])
+    for i in (0, batch - 1):
+        _check(A[i], B[i], C[i, :, :N], rows=np.arange(0, M, 3))
