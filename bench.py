@@ -159,13 +159,14 @@ def cpu_baseline(A: np.ndarray, B: np.ndarray, target_s: float = 12.0) -> dict:
     M, K = A.shape
     N = B.shape[1]
     C = np.zeros((M, N), np.float32)
+    cores = len(os.sched_getaffinity(0))
     t0 = time.perf_counter()
-    threads = oracle.sgemm_f32_cpu(A, B, C, 0, 8)
+    threads = oracle.sgemm_f32_cpu(A, B, C, 0, 8, threads=cores)
     dt = max(time.perf_counter() - t0, 1e-6)
     rate = 8 / dt  # rows per second
     rows = int(max(8, min(M, rate * target_s)))
     t0 = time.perf_counter()
-    oracle.sgemm_f32_cpu(A, B, C, 0, rows)
+    oracle.sgemm_f32_cpu(A, B, C, 0, rows, threads=cores)
     dt = time.perf_counter() - t0
     tflops = 2.0 * rows * N * K / dt / 1e12
     return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
@@ -194,19 +195,21 @@ def run_reference(args) -> None:
         A, B = synth.config5(rows=2048)
     K, N = A.shape[1], B.shape[1]
     C = np.zeros((A.shape[0], N), np.float32)
+    # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    cores = len(os.sched_getaffinity(0))
     # size one step so that warm-up + steps stay within about a minute
     t0 = time.perf_counter()
-    threads = oracle.sgemm_f32_cpu(A, B, C, 0, 8)
+    threads = oracle.sgemm_f32_cpu(A, B, C, 0, 8, threads=cores)
     rate = 8 / max(time.perf_counter() - t0, 1e-6)  # rows per second
     per_step_s = min(4.0, max(0.3, 45.0 / max(args.steps, 1)))
     rows = int(max(8, min(A.shape[0], rate * per_step_s)))
     for _ in range(args.warmup):
-        oracle.sgemm_f32_cpu(A, B, C, 0, min(rows, 8))
+        oracle.sgemm_f32_cpu(A, B, C, 0, min(rows, 8), threads=cores)
     times = []
     for s in range(args.steps):
         r0 = (s * rows) % max(A.shape[0] - rows + 1, 1)
         t0 = time.perf_counter()
-        oracle.sgemm_f32_cpu(A, B, C, r0, rows)
+        oracle.sgemm_f32_cpu(A, B, C, r0, rows, threads=cores)
         times.append(time.perf_counter() - t0)
     total = sum(times)
     tflops = 2.0 * rows * N * K * args.steps / total / 1e12
