@@ -160,8 +160,10 @@ int jst_matmul_host(const float* a, const float* b, float* c, int M, int K, int 
  * `stream` (NULL = the legacy default stream) and returns.  With pinned (page-locked) host buffers the call is
  * asynchronous and `c` is valid once the stream reaches that point; with
  * pageable buffers the copies synchronise as cudaMemcpyAsync does.  The
- * device staging buffers are per device: calls on different streams of the
- * same device must not overlap in time.
+ * device staging buffers are per device: a call on one stream waits on the
+ * GPU (not on the host) until the previous call, on any stream, has finished
+ * with them, so calls on different streams of a device take turns rather
+ * than overlap.
  */
 int jst_matmul_host_async(const float* a, const float* b, float* c, int M, int K, int N, jst_stream_t stream);
 

@@ -759,36 +759,40 @@ __global__ void split_rows_kernel(const float* __restrict__ src, int64_t ld, int
 }
 
 // Source MN-major: element (b, r, k) at src[b*sstride + k*ld + r]; transposed
-// through shared memory in tiles of 32 rows x 128 k.  Each thread issues its
-// 16 loads (32 consecutive rows per warp: 128-byte reads) before the one
-// barrier, then writes 4 consecutive k of a row as float4s (a warp covers 512
-// contiguous bytes of a plane row).  The tile row pitch of 129 floats keeps
-// the transposing shared-memory stores conflict-free.
-constexpr int STR = 32, STK = 128;
+// through shared memory in tiles of TR rows x TK k (32 x 128, or 64 x 64 when
+// K <= 64 so that no half of the block idles on padding).  Each thread issues
+// its 16 loads (32 consecutive rows per warp: 128-byte reads) before the one
+// barrier, then writes 4 consecutive k of a row as float4s (a warp covers
+// whole 16-byte chunks of plane rows).  The tile row pitch of TK + 1 floats
+// keeps the transposing shared-memory stores conflict-free.
+template <int TR, int TK>
 __global__ void __launch_bounds__(256) split_transpose_kernel(const float* __restrict__ src, int64_t ld,
                                                               int64_t sstride, int rows, int K, int Kp,
                                                               float* __restrict__ hi, float* __restrict__ lo) {
-    __shared__ float tile[STR][STK + 1];  // [row][k]
+    static_assert(TR * TK == 4096, "16 elements per thread");
+    constexpr int KT = 256 / TR;  // load phase: threads along k per pass
+    constexpr int CK = TK / 4;    // store phase: float4 chunks per tile row
+    constexpr int RP = 256 / CK;  // store phase: rows per pass
+    __shared__ float tile[TR][TK + 1];  // [row][k]
     const int b = blockIdx.z;
-    const int r0 = blockIdx.x * STR;
-    const int k0 = blockIdx.y * STK;
+    const int r0 = blockIdx.x * TR;
+    const int k0 = blockIdx.y * TK;
     const float* s = src + b * sstride;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // load phase: row fastest
-    float v[STK / 8];
+    const int tx = threadIdx.x % TR, ty = threadIdx.x / TR;  // load phase: row fastest
+    float v[TK / KT];
 #pragma unroll
-    for (int i = 0; i < STK / 8; ++i) {
-        const int k = k0 + ty + 8 * i;
+    for (int i = 0; i < TK / KT; ++i) {
+        const int k = k0 + ty + KT * i;
         const int r = r0 + tx;
         v[i] = (k < K && r < rows) ? __ldg(s + (int64_t)k * ld + r) : 0.0f;
     }
 #pragma unroll
-    for (int i = 0; i < STK / 8; ++i) tile[tx][ty + 8 * i] = v[i];
+    for (int i = 0; i < TK / KT; ++i) tile[tx][ty + KT * i] = v[i];
     __syncthreads();
-    // store phase: 32 float4 chunks per row, 8 rows per pass of 256 threads
-    const int c = threadIdx.x & 31, rr = threadIdx.x >> 5;
+    const int c = threadIdx.x % CK, rr = threadIdx.x / CK;
 #pragma unroll
-    for (int pass = 0; pass < STR / 8; ++pass) {
-        const int rl = rr + 8 * pass;
+    for (int pass = 0; pass < TR / RP; ++pass) {
+        const int rl = rr + RP * pass;
         const int r = r0 + rl;
         const int k = k0 + 4 * c;
         if (r >= rows || k >= Kp) continue;
@@ -882,10 +886,14 @@ static int launch_split(const float* src, bool kmajor, int64_t ld, int64_t sstri
             split_rows_kernel<true><<<blocks, threads, 0, s>>>(src, ld, sstride, rows, K, Kp, batch, hi, lo);
         else
             split_rows_kernel<false><<<blocks, threads, 0, s>>>(src, ld, sstride, rows, K, Kp, batch, hi, lo);
-    } else {
-        dim3 grid((rows + STR - 1) / STR, (Kp + STK - 1) / STK, batch);
+    } else if (Kp <= 64) {
+        dim3 grid((rows + 63) / 64, 1, batch);
         ProfScope prof(s, KID_SPLIT_TRANSPOSE);
-        split_transpose_kernel<<<grid, 256, 0, s>>>(src, ld, sstride, rows, K, Kp, hi, lo);
+        split_transpose_kernel<64, 64><<<grid, 256, 0, s>>>(src, ld, sstride, rows, K, Kp, hi, lo);
+    } else {
+        dim3 grid((rows + 31) / 32, (Kp + 127) / 128, batch);
+        ProfScope prof(s, KID_SPLIT_TRANSPOSE);
+        split_transpose_kernel<32, 128><<<grid, 256, 0, s>>>(src, ld, sstride, rows, K, Kp, hi, lo);
     }
     return cudaPeekAtLastError() == cudaSuccess ? JST_OK : JST_ERR_CUDA;
 }

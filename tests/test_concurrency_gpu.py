@@ -63,3 +63,26 @@ def test_threads_on_separate_streams():
     assert not any(t.is_alive() for t in threads), "a worker did not finish"
     assert not errors, errors
     assert jstorch_b200.device_error() == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(640, 384, 512), (4096, 1024, 2048)])  # direct and pipelined host paths
+def test_host_async_calls_on_two_streams_take_turns(M, K, N):
+    """Two jst_matmul_host_async calls with different inputs, enqueued back to
+    back on two streams with pinned buffers, share the device's staging
+    buffer: the second waits on the GPU for the first, and both C are right."""
+    import torch
+
+    import jstorch_b200
+    rng = np.random.default_rng(M + N)
+    ins = [(rng.standard_normal((M, K), dtype=np.float32), rng.standard_normal((K, N), dtype=np.float32))
+           for _ in range(2)]
+    pinned = [(torch.from_numpy(A).pin_memory(), torch.from_numpy(B).pin_memory(),
+               torch.full((M, N), float("nan")).pin_memory()) for A, B in ins]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for (a, b, c), st in zip(pinned, streams):
+        jstorch_b200.matmul_host_async(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, K, N, st)
+    torch.cuda.synchronize()
+    for (A, B), (_, _, c) in zip(ins, pinned):
+        rows = np.arange(0, M, max(1, M // 32))
+        err, where = oracle.max_rel_err(A, B, c.numpy(), oracle.gemm_f64(A, B, rows=rows), rows=rows)
+        assert err <= TOL, (err, where)
