@@ -491,6 +491,7 @@ def _gemm_desc(a, b, c, M, N, K, batch, *, ta=False, tb=False, sa=None, sb=None,
     (256, 128, 200, 150, True, False, False),   # A stored [K, M]: A planes from the split pass
     (384, 96, 130, 100, False, True, False),    # B stored [N, K]
     (128, 128, 288, 300, False, False, True),   # broadcast A (a convolution's weights)
+    (512, 128, 3, 100, False, False, False),    # K below one 16-wide k-slab (zero-filled tail)
 ])
 def test_persistent_narrow_tiles_match_one_tile_kernel(jst, M, N, K, batch, ta, tb, bcast_a):
     """At least one narrow output tile per SM runs the persistent kernel (one
@@ -587,3 +588,22 @@ def test_persistent_narrow_tiles_unaligned_ldc(jst):
     np.testing.assert_array_equal(C[:, :, :N], C2[:, :, :N])
     for i in (0, batch - 1):
         _check(A[i], B[i], C[i, :, :N], rows=np.arange(0, M, 3))
+
+
+def test_persistent_narrow_tiles_broadcast_b(jst):
+    """B shared by every batch entry (stride 0): its planes are split once and
+    every tile of every batch reads them."""
+    import torch
+    from jstorch_b200 import _lib
+    lib = _lib.load()
+    M, N, K, batch = 384, 96, 150, 120
+    rng = np.random.default_rng(11)
+    A, B = _rand(rng, batch, M, K), _rand(rng, K, N)
+    a, b = _dev(A), _dev(B)
+    c = torch.full((batch, M, N), float("nan"), device="cuda")
+    d = _gemm_desc(a, b, c, M, N, K, batch, sb=0)
+    _lib.check(lib.jst_gemm_ex(ctypes.byref(d)))
+    torch.cuda.synchronize()
+    C = c.cpu().numpy()
+    for i in (0, 59, batch - 1):
+        _check(A[i], B, C[i], rows=np.arange(0, M, 5))

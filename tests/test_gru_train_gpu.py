@@ -8,7 +8,10 @@ parameter gradient, dx and dh0, for L = sum(dout * output) + sum(dh_n * h_n).
 
 Bound: for each gradient tensor, max |G - G_ref| <= RTOL * max |G_ref|.  The
 GEMMs meet the path's 2e-6 bound; the gate arithmetic is fp32 and its
-rounding errors compound through the steps of the recurrence."""
+rounding errors compound through the steps of the recurrence.  Measured on a
+B200: 1e-7 .. 9e-7 for the cases below, 3.9e-6 for 8 steps and 1.4e-5 for 64
+steps at hidden 1024 (the weight gradients of the recurrent product), so
+RTOL = 1e-4 leaves about 7x margin at the longest sequence measured."""
 import numpy as np
 import pytest
 
