@@ -31,6 +31,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -1024,21 +1025,21 @@ static int launch_persist(const CUtensorMap& a_hi, const CUtensorMap& a_lo, cons
 
 // SMs of the current device (the persistent kernel's grid).
 static int sm_count() {
-    static int cached[64] = {};
+    static std::atomic<int> cached[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
         cudaGetLastError();
         return 148;
     }
-    if (!cached[dev]) {
-        int n = 0;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (!n) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = 148;
         }
-        cached[dev] = n;
+        cached[dev].store(n, std::memory_order_relaxed);
     }
-    return cached[dev];
+    return n;
 }
 
 // Narrow tiles (64 / 128 columns) in one K slice, written straight to C, and
