@@ -135,9 +135,10 @@ class ClockSampler:
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one tc_gemm
 # launch at 8192^3, from a one-pass ncu capture of this bench's own launches:
-#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none
-#       -k regex:tc_gemm -s 6 -c 1 python bench.py --steps 2 --warmup 3
-#       --no-e2e --no-cpu-baseline --no-ref-gpu
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
+#       --clock-control none -k regex:tc_gemm -s 3 -c 1 python bench.py --steps 2
+#       --warmup 3 --no-cpu-baseline --no-e2e --no-ref-gpu
+# (the first timed launch after the three warm-up calls)
 # It is not measured by the run that prints it; the line says so.
 TC_GEMM_8192_DRAM_BYTES = 4.82545e9
 
