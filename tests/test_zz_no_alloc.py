@@ -8,8 +8,9 @@ Checked through the C ABI against jst_gemm_ex (the allocating entry point,
 tensor-core kernel forced) on two calls in a row with different shapes and
 inputs, so the second call runs on scratch the first one left behind; on a
 shape that splits K (the partials live in the same array); with the device's
-free memory unchanged across calls; and with a timed-out wait (raised from
-the host) reported by jst_device_error().  This file is collected last on
+free memory unchanged across calls; with a timed-out wait (raised from the
+host) reported by jst_device_error(); and captured into a CUDA graph, whose
+replays on new inputs match the fp64 oracle and a direct call bit for bit.  This file is collected last on
 purpose; it also passes when run on its own.
 """
 import ctypes
@@ -147,3 +148,52 @@ def test_noalloc_timeout_word_is_reported_by_device_error():
     torch.cuda.synchronize()
     assert float(c.min()) == 256.0 and float(c.max()) == 256.0
     assert lib.jst_test_set_device_error(2) == 1  # JST_ERR_ARG
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 640, 768), (256, 256, 8192)])
+def test_noalloc_call_captured_in_a_cuda_graph_replays_on_new_inputs(M, N, K):
+    # The entry point's main use: after one warm-up call (module load, symbol
+    # addresses, kernel attributes) a call is captured into a CUDA graph; each
+    # replay then runs on whatever the captured input buffers hold.  The second
+    # shape splits K, so the graph also holds the partials' reduction.
+    import torch
+    lib = _lib.load()
+    rng = np.random.default_rng(M + K)
+    a = torch.empty((M, K), device="cuda")
+    b = torch.empty((K, N), device="cuda")
+    c = torch.full((M, N), float("nan"), device="cuda")
+    a.copy_(torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)))
+    b.copy_(torch.from_numpy(rng.standard_normal((K, N), dtype=np.float32)))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        d = _desc(a, b, c, M, N, K, stream=side.cuda_stream)
+        _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d)))
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        d = _desc(a, b, c, M, N, K, stream=torch.cuda.current_stream().cuda_stream)
+        _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d)))
+    try:
+        for _ in range(2):
+            A = rng.standard_normal((M, K), dtype=np.float32)
+            B = rng.standard_normal((K, N), dtype=np.float32)
+            a.copy_(torch.from_numpy(A))
+            b.copy_(torch.from_numpy(B))
+            c.fill_(float("nan"))
+            graph.replay()
+            torch.cuda.synchronize()
+            got = c.cpu().numpy()
+            ref = oracle.gemm_f64(A, B)
+            err, where = oracle.max_rel_err(A, B, got, ref)
+            assert err <= TOL, (err, where)
+            # the replay gives exactly what a direct call gives on the same inputs
+            c_direct = torch.full((M, N), float("nan"), device="cuda")
+            d2 = _desc(a, b, c_direct, M, N, K, stream=torch.cuda.current_stream().cuda_stream)
+            _lib.check(lib.jst_gemm_tc_noalloc(ctypes.byref(d2)))
+            torch.cuda.synchronize()
+            assert torch.equal(c, c_direct)
+        assert lib.jst_device_error() == 0
+    finally:
+        del graph
