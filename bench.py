@@ -133,6 +133,9 @@ class ClockSampler:
                 "samples": len(sm), "power_w_max": max(power) if power else None}
 
 
+# FP32 SIMT peak of a B200 (nominal): 148 SMs x 128 FP32 lanes x 2 flop x 1965 MHz, TFLOP/s
+FP32_SIMT_PEAK = 148 * 128 * 2 * 1965e6 / 1e12
+
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one tc_gemm
 # launch at 8192^3, from a one-pass ncu capture of this bench's own launches:
 #   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
@@ -730,7 +733,7 @@ def run_config(args) -> None:
                "value": flops / (ms * 1e-3) / 1e12, "ms": ms,
                "kernels": {k: {"launches": v[0], "avg_ms": v[1] / max(v[0], 1)} for k, v in ks.items()}}
         if args.kernel == "ffma":
-            simt_peak = 148 * 128 * 2 * 1965e6 / 1e12
+            simt_peak = FP32_SIMT_PEAK
             fk = ks.get("ffma_gemm", (1, ms))
             ach = flops / (fk[1] / max(fk[0], 1) * 1e-3) / 1e12
             res["roofline"] = {"kernel": "ffma_gemm", "bound": "fma", "achieved": ach, "peak": simt_peak,
@@ -1115,14 +1118,19 @@ def run_jstorch(args) -> None:
     kernel_ms = tot / max(nl, 1)
     achieved = flops / (kernel_ms * 1e-3) / 1e12 if kernel_ms > 0 else None
     full_size = M == SIZE and args.kernel in ("auto", "tc3xtf32")
-    roofline = {"kernel": name, "bound": "tensor", "achieved": achieved, "peak": peak,
+    bound, peak_note = "tensor", f"3xTF32 roofline = {peak_kind} / 2 (TF32 rate) / 3 (three products)"
+    if name == "ffma_gemm":  # the SIMT kernel: FP32 FMA pipe, not the tensor cores
+        bound, peak = "fma", FP32_SIMT_PEAK
+        burst = FP32_SIMT_PEAK
+        peak_note = "FP32 SIMT peak 148 SMs x 128 lanes x 2 flop x 1965 MHz (nominal)"
+    roofline = {"kernel": name, "bound": bound, "achieved": achieved, "peak": peak,
                 "unit": "TFLOP/s", "frac": (achieved / peak) if achieved else None,
                 "frac_of_burst": (achieved / burst) if achieved else None,
                 "traffic": TC_GEMM_8192_DRAM_BYTES if full_size else None,
                 "traffic_source": ("one ncu capture of a bench tc_gemm launch at 8192^3 with the command in "
                                    "bench.py (not measured by this run)") if full_size else None,
                 "algorithmic_bytes": 4.0 * (2 * (M + N) * ((K + 3) // 4 * 4) + M * N),
-                "peak_note": f"3xTF32 roofline = {peak_kind} / 2 (TF32 rate) / 3 (three products)",
+                "peak_note": peak_note,
                 "kernel_ms": kernel_ms,
                 "kernel_timing": f"CUDA events around each launch on its stream, {prof_steps} calls after a "
                                  f"{REST_S} s pause (clocks: {pclk.get('sm_mhz')} MHz median, "

@@ -12,7 +12,8 @@
 // shared memory (double buffered; the next tile is fetched into registers
 // while the current one is multiplied).  Global loads are float4 whenever
 // the operand's leading dimension and base allow it, scalar and bounds-checked
-// elsewhere.
+// elsewhere; tiles wholly inside M x N with aligned operands skip the
+// per-element checks for every full k-slab.
 //
 // Split K: when the tiles of C cannot fill the SMs (the M = 256 layers of an
 // MLP, 512^3), K is cut into S slices of whole BK steps; CTA (tile, slice)
@@ -82,8 +83,35 @@ __global__ void __launch_bounds__((BM / (4 * RM)) * (BN / (4 * RN)), 2)
 
     float ra[LA][4], rb[LB][4];
 
+    // Interior tiles of float4-aligned operands load whole k-slabs with no
+    // per-element bounds checks (a uniform branch per slab).
+    const bool interior = p.vecA && p.vecB && m0 + BM <= p.M && n0 + BN <= p.N;
+
     // Fetch the k-slab starting at k0 into registers.
     auto fetch = [&](int k0) {
+        if (interior && k0 + BK <= kend) {
+#pragma unroll
+            for (int l = 0; l < LA; ++l) {
+                const int f = tid + l * NT;
+                if (f >= A4) break;
+                const int r = !TA ? f / (BK / 4) : f / (BM / 4);
+                const int c = !TA ? (f % (BK / 4)) * 4 : (f % (BM / 4)) * 4;
+                const float* src = A + (int64_t)((!TA ? m0 : k0) + r) * p.lda + (!TA ? k0 : m0) + c;
+                const float4 v = __ldg(reinterpret_cast<const float4*>(src));
+                ra[l][0] = v.x; ra[l][1] = v.y; ra[l][2] = v.z; ra[l][3] = v.w;
+            }
+#pragma unroll
+            for (int l = 0; l < LB; ++l) {
+                const int f = tid + l * NT;
+                if (f >= B4) break;
+                const int r = !TB ? f / (BN / 4) : f / (BK / 4);
+                const int c = !TB ? (f % (BN / 4)) * 4 : (f % (BK / 4)) * 4;
+                const float* src = B + (int64_t)((!TB ? k0 : n0) + r) * p.ldb + (!TB ? n0 : k0) + c;
+                const float4 v = __ldg(reinterpret_cast<const float4*>(src));
+                rb[l][0] = v.x; rb[l][1] = v.y; rb[l][2] = v.z; rb[l][3] = v.w;
+            }
+            return;
+        }
 #pragma unroll
         for (int l = 0; l < LA; ++l) {
             const int f = tid + l * NT;
