@@ -153,7 +153,19 @@ __global__ void __launch_bounds__(THREADS, C::MIN_BLOCKS)
     const int first_m = g * GROUP;
     const int gm = min(p.tiles_m - first_m, GROUP);
     const int tm = first_m + (t % group_span) % gm;
-    const int tn = (t % group_span) / gm;
+    const int tn_band = (t % group_span) / gm;
+    // Wide tiles (one CTA per SM, so a wave is 148 consecutive CTAs): the
+    // waves of a band share their A panels, which are larger than L2.  The
+    // CTAs of odd waves walk K downwards, so a wave starts on the k-slabs the
+    // previous wave read last and still finds them in L2, while the CTAs of
+    // one wave keep moving through K together (sharing their k-slabs); odd
+    // bands walk the tile columns backwards, so a band starts on the B panels
+    // the previous band ended on.  Each output still sums its K steps in one
+    // fixed order (set by its CTA index), so results repeat bit for bit.
+    constexpr int WAVE = 148;
+    const bool wide_order = BN == 256 && p.kslices == 1;
+    const int tn = (wide_order && (g & 1)) ? p.tiles_n - 1 - tn_band : tn_band;
+    const bool k_down = wide_order && ((blockIdx.x / WAVE) & 1);
     const int m0 = tm * BM;
     const int n0 = tn * BN;
     const int kb0 = slice * p.kb_per_slice;  // this CTA's K steps: [kb0, kb0 + num_kb)
@@ -193,7 +205,7 @@ __global__ void __launch_bounds__(THREADS, C::MIN_BLOCKS)
                 if (!ptx::mbar_wait(&empty_bar[s], phase ^ 1, err)) break;
                 uint8_t* st = smem + s * STAGE_BYTES;
                 ptx::mbar_arrive_expect_tx(&full_bar[s], p.split_a ? STAGE_BYTES - A_TILE_BYTES : STAGE_BYTES);
-                const int kx = (kb0 + kb) * BK;
+                const int kx = (kb0 + (k_down ? num_kb - 1 - kb : kb)) * BK;
                 ptx::tma_load_3d(st, &tm_a_hi, &full_bar[s], kx, m0, za);  // split_a: the raw fp32 tile
                 if (!p.split_a) ptx::tma_load_3d(st + A_TILE_BYTES, &tm_a_lo, &full_bar[s], kx, m0, za);
                 ptx::tma_load_3d(st + 2 * A_TILE_BYTES, &tm_b_hi, &full_bar[s], kx, n0, zb);
