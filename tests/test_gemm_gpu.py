@@ -607,3 +607,26 @@ def test_persistent_narrow_tiles_broadcast_b(jst):
     C = c.cpu().numpy()
     for i in (0, 59, batch - 1):
         _check(A[i], B, C[i], rows=np.arange(0, M, 5))
+
+
+@pytest.mark.parametrize("K", [1000, 1024])
+def test_wide_tiles_over_two_waves_and_two_bands(jst, K):
+    """2304 x 2304 output in 128 x 256 tiles: 162 one-CTA-per-SM tiles, so
+    CTAs 148-161 form a second wave that walks K downwards, and the two tile
+    rows past the first band of 16 walk their columns backwards.  K = 1000
+    ends on a partial k-slab, which those CTAs load first (zero-filled past
+    K).  Rows from both bands and every wave are checked against the fp64
+    oracle, and a second run must give the same bits."""
+    import torch
+    rng = np.random.default_rng(K)
+    M = N = 2304
+    A = _rand(rng, M, K)
+    B = _rand(rng, K, N)
+    a, b = _dev(A), _dev(B)
+    c1 = jst.gemm(a, b, kernel="tc3xtf32")
+    c2 = jst.gemm(a, b, kernel="tc3xtf32")
+    torch.cuda.synchronize()
+    C = c1.cpu().numpy()
+    np.testing.assert_array_equal(C, c2.cpu().numpy())
+    rows = np.unique(np.concatenate([np.arange(0, M, 37), np.arange(2048, M, 7), [M - 1]]))
+    _check(A, B, C, rows=rows)
